@@ -1,0 +1,244 @@
+/*
+ * mhc_b200.h — C ABI of the B200 (sm_100a) mHC residual-path kernels.
+ *
+ * Drop-in boundary for the manifold-constrained hyper-connection (mHC) layer of
+ * Tshirt-hfk/minimind-mhc.  Every entry point replaces one kernel launch (plus
+ * the torch reductions around it) that the reference performs inside its
+ * autograd Functions; the citation beside each declaration names the reference
+ * lines it replaces (paths relative to the reference project root).
+ *
+ * Conventions
+ *  - Plain device pointers, element counts and dtype codes; no framework types.
+ *  - Activations are row-major: x is (T, n*C) with the n streams of a token
+ *    stored one after the other (stream i at columns [i*C, (i+1)*C)), z and f
+ *    are (T, C), per-token coefficient tensors are (T, n) and (T, n, n).
+ *  - phi is (n*C, FD) row-major, exactly the layout of the reference's
+ *    `phi_weight` parameter (model/mhc_fused.py:798).
+ *  - `stream` is a cudaStream_t passed as void*.  Nothing here synchronises,
+ *    allocates device memory or keeps per-call host state; scratch memory is
+ *    the caller's `workspace` (size from the matching *_workspace() query).
+ *  - Every call validates its arguments before launching and returns MHC_OK or
+ *    a negative status; `mhc_last_error()` gives a message for the calling
+ *    thread.  A call that returns an error launched nothing.
+ *  - Kernels are reentrant: calls on different streams with disjoint buffers
+ *    may run concurrently.
+ */
+#ifndef MHC_B200_H
+#define MHC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define MHC_F32  0
+#define MHC_BF16 1
+#define MHC_F16  2
+
+/* status codes */
+#define MHC_OK               0
+#define MHC_ERR_NULL        -1  /* a required pointer is NULL                  */
+#define MHC_ERR_DTYPE       -2  /* unsupported dtype code                      */
+#define MHC_ERR_SHAPE       -3  /* unsupported n, C, T, iteration count        */
+#define MHC_ERR_ALIGN       -4  /* pointer misaligned for the required access  */
+#define MHC_ERR_WORKSPACE   -5  /* workspace missing or too small              */
+#define MHC_ERR_CUDA        -6  /* CUDA launch / runtime failure               */
+#define MHC_ERR_UNSUPPORTED -7  /* combination not implemented                 */
+
+/* Version of this ABI (bumped on any signature change). */
+int mhc_abi_version(void);
+
+/* Message describing the last failing call on the calling thread ("" if none). */
+const char *mhc_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Forward: coefficients (+ Sinkhorn) and the pre-aggregate                 */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of scratch `mhc_pre_fwd` needs for T tokens. */
+size_t mhc_pre_fwd_workspace(int64_t T, int n, int C, int with_res);
+
+/*
+ * Coefficient kernel + pre-aggregate of one mHC sublayer.
+ *
+ *   inv_rms[t] = 1/sqrt(mean_k x[t,k]^2 + rms_eps)            (fp32, required)
+ *   mixes[t,:] = inv_rms[t] * (x[t,:] @ phi)                  (fp32, required, FD wide)
+ *   h_pre      = sigmoid(alpha_pre*mixes[:, :n] + bias_pre) + pre_eps
+ *   h_post     = sigmoid(alpha_post*mixes[:, n:2n] + bias_post) * post_mult
+ *   h_res      = alpha_res*mixes[:, 2n:].view(n,n) + bias_res         (apply_sinkhorn == 0)
+ *              = Sinkhorn(that, sinkhorn_iters, sinkhorn_eps)         (apply_sinkhorn != 0)
+ *   z[t,c]     = sum_i h_pre[t,i] * x[t, i*C + c]
+ *
+ * with_res = 1: full mHC (FD = 2n + n^2);  with_res = 0: no-H_res variant
+ * (FD = 2n; alpha_res, bias_res, h_res ignored and may be NULL).
+ * h_pre, h_post, h_res are written in `coef_dtype` and may be NULL when not
+ * wanted; z is written in x_dtype.  Parameters (phi, alphas, biases) are read
+ * in `param_dtype` and converted to fp32; all coefficient math is fp32.
+ *
+ * Replaces: model/mhc_fused.py:615-625 (_pre_phase_full_fwd_kernel launch in
+ * _PrePhaseFullFn.forward) and, with apply_sinkhorn, model/mhc_fused.py:120-123
+ * (_sinkhorn_fwd_kernel launch in _SinkhornFn.forward); with with_res = 0,
+ * model/mhc_fused_no_hres.py:440-449 (_pre_phase_fwd_kernel launch).
+ */
+int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C,
+                const void *phi, const void *alpha_pre, const void *bias_pre,
+                const void *alpha_post, const void *bias_post,
+                const void *alpha_res, const void *bias_res, int param_dtype,
+                int with_res, int apply_sinkhorn, int sinkhorn_iters,
+                float post_mult, float pre_eps, float rms_eps, float sinkhorn_eps,
+                void *z, void *h_pre, void *h_post, void *h_res, int coef_dtype,
+                float *inv_rms, float *mixes,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Forward: post / res merge                                                 */
+/* ------------------------------------------------------------------------ */
+
+/*
+ *   out[t, i*C + c] = sum_j h_res[t,i,j] * x[t, j*C + c] + h_post[t,i] * f[t,c]
+ * h_res == NULL means H_res = I (no-H_res variant: out = x + h_post (x) f).
+ * out has x_dtype.
+ *
+ * Replaces: model/mhc_fused.py:736-739 (_post_phase_full_fwd_kernel launch) and
+ * model/mhc_fused_no_hres.py:547-550 (_post_phase_fwd_kernel launch).
+ */
+int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype,
+                 const void *h_post, int h_post_dtype, const void *f, int f_dtype,
+                 void *out, int64_t T, int n, int C, void *stream);
+
+/*
+ * Backward of mhc_post_fwd for upstream gradient dout (x_dtype):
+ *   dx[t, j*C+c]  = sum_i h_res[t,i,j] * dout[t, i*C+c]     (= dout when h_res == NULL)
+ *   dh_res[t,i,j] = sum_c dout[t, i*C+c] * x[t, j*C+c]      (h_res_dtype)
+ *   dh_post[t,i]  = sum_c dout[t, i*C+c] * f[t,c]          (h_post_dtype)
+ *   df[t,c]       = sum_i h_post[t,i] * dout[t, i*C+c]     (f_dtype)
+ * Any output pointer may be NULL to skip it (dh_res must be NULL when h_res is).
+ *
+ * Replaces: model/mhc_fused.py:761-766 (_post_phase_full_bwd_kernel launch) and
+ * model/mhc_fused_no_hres.py:572-576 (_post_phase_bwd_kernel launch).
+ */
+int mhc_post_bwd(const void *dout, const void *x, int x_dtype,
+                 const void *h_res, int h_res_dtype, const void *h_post, int h_post_dtype,
+                 const void *f, int f_dtype,
+                 void *dx, void *dh_res, void *dh_post, void *df,
+                 int64_t T, int n, int C, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Backward: coefficients (+ Sinkhorn by recompute) and pre-aggregate        */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of scratch `mhc_pre_bwd` needs for T tokens with the same with_res /
+ * apply_sinkhorn / sinkhorn_iters arguments.  The answer depends on the SM count
+ * of the current device: query on the device the call will run on. */
+size_t mhc_pre_bwd_workspace(int64_t T, int n, int C, int with_res, int apply_sinkhorn,
+                             int sinkhorn_iters);
+
+/*
+ * Backward of mhc_pre_fwd.  Inputs: x, phi, parameters, the saved fp32
+ * inv_rms (T) and mixes (T, FD), and the upstream gradients dz (x_dtype),
+ * dh_pre / dh_post / dh_res (coef_dtype, each may be NULL = zero).
+ * apply_sinkhorn != 0: dh_res is the gradient w.r.t. the Sinkhorn OUTPUT and the
+ * Sinkhorn backward runs by recompute from mixes; otherwise dh_res is the
+ * gradient w.r.t. the raw logits.  dx_add (x_dtype, may be NULL) is added into
+ * dx (fuses the residual-gradient sum autograd would otherwise do in a separate
+ * pass).  Outputs: dx (x_dtype), dphi (n*C, FD) and the alpha/bias gradients in
+ * param_dtype (any may be NULL to skip; the res ones must be NULL when
+ * with_res = 0).  Parameter gradients are reduced over tokens deterministically
+ * (fixed-order two-pass reduction, no atomics).
+ *
+ * Replaces: model/mhc_fused.py:681-711 (_pre_phase_full_bwd_kernel launch, the
+ * cuBLAS grad_W GEMM and the torch alpha/bias reductions), with apply_sinkhorn
+ * also model/mhc_fused.py:131-137 (_SinkhornFn.backward), and
+ * model/mhc_fused_no_hres.py:500-524 for with_res = 0.
+ */
+int mhc_pre_bwd(const void *x, int x_dtype, int64_t T, int n, int C,
+                const void *phi, const void *alpha_pre, const void *bias_pre,
+                const void *alpha_post, const void *bias_post,
+                const void *alpha_res, const void *bias_res, int param_dtype,
+                int with_res, int apply_sinkhorn, int sinkhorn_iters,
+                float post_mult, float pre_eps, float rms_eps, float sinkhorn_eps,
+                const float *inv_rms, const float *mixes,
+                const void *dz, const void *dh_pre, const void *dh_post, const void *dh_res,
+                int coef_dtype, const void *dx_add,
+                void *dx, void *dphi, void *dalpha_pre, void *dbias_pre,
+                void *dalpha_post, void *dbias_post, void *dalpha_res, void *dbias_res,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Stand-alone Sinkhorn-Knopp                                                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Y[b] = Sinkhorn(M[b]) for `batch` n x n matrices: row softmax + eps, one
+ * column normalisation, then (iters-1) row/column normalisations, each
+ * dividing by (sum + eps).  Math in fp32.
+ * Replaces: model/mhc_fused.py:120-123 (_sinkhorn_fwd_kernel launch).
+ */
+int mhc_sinkhorn_fwd(const void *M, int m_dtype, void *Y, int y_dtype,
+                     int64_t batch, int n, int iters, float eps, void *stream);
+
+/*
+ * dM = d Sinkhorn(M) / dM applied to dY, by recomputing the forward
+ * trajectory.  Replaces: model/mhc_fused.py:131-137 (_SinkhornFn.backward).
+ */
+int mhc_sinkhorn_bwd(const void *M, int m_dtype, const void *dY, int dy_dtype,
+                     void *dM, int dm_dtype, int64_t batch, int n, int iters, float eps,
+                     void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Model exit (MHCHead) and entry (StreamExpand)                             */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of scratch `mhc_head_fwd` needs for T tokens. */
+size_t mhc_head_fwd_workspace(int64_t T, int n, int C);
+
+/*
+ * MHCHead: out[t,c] = sum_i w[t,i] x[t, i*C+c], w = sigmoid(alpha*mix + bias) + pre_eps,
+ * mix = inv_rms * (x @ phi) with phi (n*C, n).  n == 1: out = x * inv_rms
+ * (plain unweighted RMSNorm, phi/alpha/bias unused, mix_raw may be NULL).
+ * inv_rms (T) and mix_raw (T, n) are fp32 saved tensors.
+ * Replaces: model/mhc_common.py:344-351 (_mhc_head_fwd_kernel launch) and the
+ * n == 1 branch model/mhc_common.py:438-442.
+ */
+int mhc_head_fwd(const void *x, int x_dtype, int64_t T, int n, int C,
+                 const void *phi, const void *alpha, const void *bias, int param_dtype,
+                 float pre_eps, float rms_eps,
+                 void *out, float *inv_rms, float *mix_raw,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of scratch `mhc_head_bwd` needs for T tokens (current device). */
+size_t mhc_head_bwd_workspace(int64_t T, int n, int C);
+
+/*
+ * Backward of mhc_head_fwd: dx (x_dtype), dphi / dalpha / dbias (param_dtype,
+ * may be NULL; unused for n == 1).
+ * Replaces: model/mhc_common.py:377-395 (_mhc_head_bwd_kernel launch, cuBLAS
+ * grad_W and the torch alpha/bias reductions).
+ */
+int mhc_head_bwd(const void *x, int x_dtype, int64_t T, int n, int C,
+                 const void *phi, const void *alpha, const void *bias, int param_dtype,
+                 float pre_eps, float rms_eps, const float *inv_rms, const float *mix_raw,
+                 const void *dout, void *dx, void *dphi, void *dalpha, void *dbias,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * StreamExpand: out[t, i*C + c] = x[t, c] for i < n.  Backward: dx[t,c] =
+ * sum_i dout[t, i*C + c].  Replaces: model/mhc_common.py:115-119 (expand +
+ * reshape copy) and its autograd.
+ */
+int mhc_stream_expand_fwd(const void *x, void *out, int dtype, int64_t T, int n, int C,
+                          void *stream);
+int mhc_stream_expand_bwd(const void *dout, void *dx, int dtype, int64_t T, int n, int C,
+                          void *stream);
+
+/* Number of SMs of the current device (cached per device); <0 on error. */
+int mhc_device_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHC_B200_H */

@@ -1,0 +1,329 @@
+// C ABI entry points (include/mhc_b200.h): argument validation, workspace
+// carving and dispatch to the kernel launchers.  No entry point allocates,
+// synchronises or launches anything when its arguments are rejected.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "mhc_b200.h"
+#include "mhc_dispatch.cuh"
+#include "mhc_kernels.h"
+
+namespace mhc {
+
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_status(cudaError_t e, const char *where) {
+  if (e == cudaSuccess) return MHC_OK;
+  return fail(MHC_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+int device_sm_count() {
+  static int cache[128] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return -1;
+  if (dev < 128 && cache[dev] > 0) return cache[dev];
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (dev < 128) cache[dev] = v;
+  return v;
+}
+
+static bool dtype_ok(int d) { return d == MHC_F32 || d == MHC_BF16 || d == MHC_F16; }
+static bool n_ok(int n) { return n == 1 || n == 2 || n == 4 || n == 8 || n == 16; }
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+static bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+static size_t esize(int d) { return d == MHC_F32 ? 4 : 2; }
+
+static int check_shape(int64_t T, int n, int C) {
+  if (T < 0) return fail(MHC_ERR_SHAPE, "T must be >= 0 (got %lld)", (long long)T);
+  if (!n_ok(n)) return fail(MHC_ERR_SHAPE, "n must be one of 1,2,4,8,16 (got %d)", n);
+  if (C < 1) return fail(MHC_ERR_SHAPE, "C must be >= 1 (got %d)", C);
+  if ((int64_t)n * C > (int64_t)1 << 30) return fail(MHC_ERR_SHAPE, "n*C too large");
+  return MHC_OK;
+}
+
+static int check_elem_align(const void *p, int dtype, const char *name) {
+  if (p && !aligned(p, esize(dtype))) return fail(MHC_ERR_ALIGN, "%s is not %zu-byte aligned", name, esize(dtype));
+  return MHC_OK;
+}
+
+}  // namespace mhc
+
+using namespace mhc;
+
+#define MHC_TRY(expr)           \
+  do {                          \
+    const int _s = (expr);      \
+    if (_s != MHC_OK) return _s; \
+  } while (0)
+
+extern "C" {
+
+int mhc_abi_version(void) { return 1; }
+
+const char *mhc_last_error(void) { return g_err; }
+
+int mhc_device_sm_count(void) { return device_sm_count(); }
+
+size_t mhc_pre_fwd_workspace(int64_t T, int n, int C, int with_res) {
+  (void)C;
+  (void)with_res;
+  if (T <= 0 || n <= 0) return 256;
+  return align256((size_t)T * n * 4);
+}
+
+int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void *phi,
+                const void *alpha_pre, const void *bias_pre, const void *alpha_post,
+                const void *bias_post, const void *alpha_res, const void *bias_res, int param_dtype,
+                int with_res, int apply_sinkhorn, int sinkhorn_iters, float post_mult,
+                float pre_eps, float rms_eps, float sinkhorn_eps, void *z, void *h_pre,
+                void *h_post, void *h_res, int coef_dtype, float *inv_rms, float *mixes,
+                void *workspace, size_t workspace_bytes, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(param_dtype) || !dtype_ok(coef_dtype))
+    return fail(MHC_ERR_DTYPE, "mhc_pre_fwd: bad dtype code (x=%d param=%d coef=%d)", x_dtype,
+                param_dtype, coef_dtype);
+  if (with_res != 0 && with_res != 1) return fail(MHC_ERR_SHAPE, "with_res must be 0 or 1");
+  if (sinkhorn_iters < 0 || sinkhorn_iters > 100000) return fail(MHC_ERR_SHAPE, "bad sinkhorn_iters %d", sinkhorn_iters);
+  if (T == 0) return MHC_OK;
+  if (!x || !phi || !alpha_pre || !bias_pre || !alpha_post || !bias_post || !z || !inv_rms || !mixes)
+    return fail(MHC_ERR_NULL, "mhc_pre_fwd: required pointer is NULL");
+  if (with_res && (!alpha_res || !bias_res)) return fail(MHC_ERR_NULL, "mhc_pre_fwd: alpha_res/bias_res NULL");
+  const size_t need = mhc_pre_fwd_workspace(T, n, C, with_res);
+  if (!workspace || workspace_bytes < need)
+    return fail(MHC_ERR_WORKSPACE, "mhc_pre_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (!aligned(workspace, 16) || !aligned(inv_rms, 4) || !aligned(mixes, 4))
+    return fail(MHC_ERR_ALIGN, "mhc_pre_fwd: workspace/inv_rms/mixes misaligned");
+  MHC_TRY(check_elem_align(x, x_dtype, "x"));
+  MHC_TRY(check_elem_align(z, x_dtype, "z"));
+  CoefParams p{alpha_pre, bias_pre, alpha_post, bias_post, alpha_res, bias_res, param_dtype,
+               post_mult, pre_eps, rms_eps, sinkhorn_eps, apply_sinkhorn ? 1 : 0, sinkhorn_iters};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float *gate = reinterpret_cast<float *>(workspace);
+  const int mode = with_res ? 0 : 1;
+  MHC_TRY(cuda_status(launch_coef_fwd(mode, n, x_dtype, x, T, C, phi, p, h_pre, h_post,
+                                      with_res ? h_res : nullptr, coef_dtype, inv_rms, mixes, gate,
+                                      device_sm_count(), s),
+                      "mhc_pre_fwd coef"));
+  return cuda_status(launch_aggregate(n, x_dtype, x, gate, z, T, C, s), "mhc_pre_fwd aggregate");
+}
+
+int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype, const void *h_post,
+                 int h_post_dtype, const void *f, int f_dtype, void *out, int64_t T, int n, int C,
+                 void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(h_post_dtype) || !dtype_ok(f_dtype) ||
+      (h_res && !dtype_ok(h_res_dtype)))
+    return fail(MHC_ERR_DTYPE, "mhc_post_fwd: bad dtype code");
+  if (T == 0) return MHC_OK;
+  if (!x || !h_post || !f || !out) return fail(MHC_ERR_NULL, "mhc_post_fwd: required pointer is NULL");
+  MHC_TRY(check_elem_align(x, x_dtype, "x"));
+  MHC_TRY(check_elem_align(out, x_dtype, "out"));
+  MHC_TRY(check_elem_align(f, f_dtype, "f"));
+  return cuda_status(launch_post_fwd(n, x_dtype, x, h_res, h_res_dtype, h_post, h_post_dtype, f,
+                                     f_dtype, out, T, C, reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_post_fwd");
+}
+
+int mhc_post_bwd(const void *dout, const void *x, int x_dtype, const void *h_res, int h_res_dtype,
+                 const void *h_post, int h_post_dtype, const void *f, int f_dtype, void *dx,
+                 void *dh_res, void *dh_post, void *df, int64_t T, int n, int C, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(h_post_dtype) || !dtype_ok(f_dtype) ||
+      (h_res && !dtype_ok(h_res_dtype)))
+    return fail(MHC_ERR_DTYPE, "mhc_post_bwd: bad dtype code");
+  if (!h_res && dh_res) return fail(MHC_ERR_NULL, "mhc_post_bwd: dh_res given without h_res");
+  if (T == 0) return MHC_OK;
+  if (!dout || !h_post || !f) return fail(MHC_ERR_NULL, "mhc_post_bwd: required pointer is NULL");
+  if (h_res && !x) return fail(MHC_ERR_NULL, "mhc_post_bwd: x required with h_res");
+  MHC_TRY(check_elem_align(dout, x_dtype, "dout"));
+  MHC_TRY(check_elem_align(x, x_dtype, "x"));
+  MHC_TRY(check_elem_align(dx, x_dtype, "dx"));
+  MHC_TRY(check_elem_align(df, f_dtype, "df"));
+  return cuda_status(launch_post_bwd(n, x_dtype, dout, x ? x : dout, h_res, h_res_dtype, h_post,
+                                     h_post_dtype, f, f_dtype, dx, dh_res, dh_post, df, T, C,
+                                     reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_post_bwd");
+}
+
+size_t mhc_pre_bwd_workspace(int64_t T, int n, int C, int with_res, int apply_sinkhorn,
+                             int sinkhorn_iters) {
+  if (T < 0 || !n_ok(n) || C < 1) return 0;
+  const int mode = with_res ? 0 : 1;
+  return plan_pre_bwd(mode, n, T, C, apply_sinkhorn ? sinkhorn_iters : 0, device_sm_count()).total;
+}
+
+static int pre_bwd_common(int mode, const void *x, int x_dtype, int64_t T, int n, int C,
+                          const void *phi, const CoefParams &p, const float *inv_rms,
+                          const float *mixes, const void *dz, const void *dh_pre,
+                          const void *dh_post, const void *dh_res, int coef_dtype,
+                          const void *dx_add, void *dx, void *dphi, void *da_pre, void *db_pre,
+                          void *da_post, void *db_post, void *da_res, void *db_res,
+                          void *workspace, size_t workspace_bytes, void *stream, const char *who) {
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(p.param_dtype) || !dtype_ok(coef_dtype))
+    return fail(MHC_ERR_DTYPE, "%s: bad dtype code", who);
+  if (p.sk_iters < 0 || p.sk_iters > 100000) return fail(MHC_ERR_SHAPE, "%s: bad sinkhorn_iters", who);
+  const PreBwdPlan plan = plan_pre_bwd(mode, n, T, C, (mode == 0 && p.apply_sinkhorn) ? p.sk_iters : 0,
+                                       device_sm_count());
+  if (plan.k1_tokens <= 0)
+    return fail(MHC_ERR_UNSUPPORTED, "%s: Sinkhorn trajectory of %d iterations does not fit in shared memory", who,
+                p.sk_iters);
+  if (T > 0) {
+    if (!x || !phi || !inv_rms || !mixes || !dz || !dx)
+      return fail(MHC_ERR_NULL, "%s: required pointer is NULL", who);
+    MHC_TRY(check_elem_align(x, x_dtype, "x"));
+    MHC_TRY(check_elem_align(dz, x_dtype, "dz"));
+    MHC_TRY(check_elem_align(dx, x_dtype, "dx"));
+    MHC_TRY(check_elem_align(dx_add, x_dtype, "dx_add"));
+  }
+  if (!workspace || workspace_bytes < plan.total)
+    return fail(MHC_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, plan.total);
+  if (!aligned(workspace, 256)) return fail(MHC_ERR_ALIGN, "%s: workspace must be 256-byte aligned", who);
+  return cuda_status(launch_pre_bwd(mode, n, x_dtype, x, T, C, phi, p, inv_rms, mixes, dz, dh_pre,
+                                    dh_post, dh_res, coef_dtype, dx_add, dx, dphi, da_pre, db_pre,
+                                    da_post, db_post, da_res, db_res, workspace, plan,
+                                    reinterpret_cast<cudaStream_t>(stream)),
+                     who);
+}
+
+int mhc_pre_bwd(const void *x, int x_dtype, int64_t T, int n, int C, const void *phi,
+                const void *alpha_pre, const void *bias_pre, const void *alpha_post,
+                const void *bias_post, const void *alpha_res, const void *bias_res, int param_dtype,
+                int with_res, int apply_sinkhorn, int sinkhorn_iters, float post_mult,
+                float pre_eps, float rms_eps, float sinkhorn_eps, const float *inv_rms,
+                const float *mixes, const void *dz, const void *dh_pre, const void *dh_post,
+                const void *dh_res, int coef_dtype, const void *dx_add, void *dx, void *dphi,
+                void *dalpha_pre, void *dbias_pre, void *dalpha_post, void *dbias_post,
+                void *dalpha_res, void *dbias_res, void *workspace, size_t workspace_bytes,
+                void *stream) {
+  g_err[0] = 0;
+  if (with_res != 0 && with_res != 1) return fail(MHC_ERR_SHAPE, "with_res must be 0 or 1");
+  if (T > 0 && (!alpha_pre || !bias_pre || !alpha_post || !bias_post))
+    return fail(MHC_ERR_NULL, "mhc_pre_bwd: parameter pointer is NULL");
+  if (with_res && T > 0 && (!alpha_res || !bias_res)) return fail(MHC_ERR_NULL, "mhc_pre_bwd: alpha_res/bias_res NULL");
+  if (!with_res && (dh_res || dalpha_res || dbias_res))
+    return fail(MHC_ERR_NULL, "mhc_pre_bwd: res gradients given with with_res = 0");
+  CoefParams p{alpha_pre, bias_pre, alpha_post, bias_post, alpha_res, bias_res, param_dtype,
+               post_mult, pre_eps, rms_eps, sinkhorn_eps, apply_sinkhorn ? 1 : 0, sinkhorn_iters};
+  return pre_bwd_common(with_res ? 0 : 1, x, x_dtype, T, n, C, phi, p, inv_rms, mixes, dz, dh_pre,
+                        dh_post, with_res ? dh_res : nullptr, coef_dtype, dx_add, dx, dphi,
+                        dalpha_pre, dbias_pre, dalpha_post, dbias_post, dalpha_res, dbias_res,
+                        workspace, workspace_bytes, stream, "mhc_pre_bwd");
+}
+
+int mhc_sinkhorn_fwd(const void *M, int m_dtype, void *Y, int y_dtype, int64_t batch, int n,
+                     int iters, float eps, void *stream) {
+  g_err[0] = 0;
+  if (batch < 0 || !n_ok(n)) return fail(MHC_ERR_SHAPE, "mhc_sinkhorn_fwd: bad batch/n");
+  if (!dtype_ok(m_dtype) || !dtype_ok(y_dtype)) return fail(MHC_ERR_DTYPE, "mhc_sinkhorn_fwd: bad dtype");
+  if (iters < 0 || iters > 100000) return fail(MHC_ERR_SHAPE, "mhc_sinkhorn_fwd: bad iters");
+  if (batch == 0) return MHC_OK;
+  if (!M || !Y) return fail(MHC_ERR_NULL, "mhc_sinkhorn_fwd: NULL pointer");
+  return cuda_status(launch_sinkhorn_fwd(n, M, m_dtype, Y, y_dtype, batch, iters, eps,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_sinkhorn_fwd");
+}
+
+int mhc_sinkhorn_bwd(const void *M, int m_dtype, const void *dY, int dy_dtype, void *dM,
+                     int dm_dtype, int64_t batch, int n, int iters, float eps, void *stream) {
+  g_err[0] = 0;
+  if (batch < 0 || !n_ok(n)) return fail(MHC_ERR_SHAPE, "mhc_sinkhorn_bwd: bad batch/n");
+  if (!dtype_ok(m_dtype) || !dtype_ok(dy_dtype) || !dtype_ok(dm_dtype))
+    return fail(MHC_ERR_DTYPE, "mhc_sinkhorn_bwd: bad dtype");
+  if (iters < 0 || iters > 100000) return fail(MHC_ERR_SHAPE, "mhc_sinkhorn_bwd: bad iters");
+  if (sinkhorn_bwd_smem_per_item(n, iters) > 200 * 1024)
+    return fail(MHC_ERR_UNSUPPORTED, "mhc_sinkhorn_bwd: trajectory too large for shared memory");
+  if (batch == 0) return MHC_OK;
+  if (!M || !dY || !dM) return fail(MHC_ERR_NULL, "mhc_sinkhorn_bwd: NULL pointer");
+  return cuda_status(launch_sinkhorn_bwd(n, M, m_dtype, dY, dy_dtype, dM, dm_dtype, batch, iters, eps,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_sinkhorn_bwd");
+}
+
+size_t mhc_head_fwd_workspace(int64_t T, int n, int C) { return mhc_pre_fwd_workspace(T, n, C, 0); }
+
+int mhc_head_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void *phi,
+                 const void *alpha, const void *bias, int param_dtype, float pre_eps, float rms_eps,
+                 void *out, float *inv_rms, float *mix_raw, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(param_dtype)) return fail(MHC_ERR_DTYPE, "mhc_head_fwd: bad dtype");
+  if (T == 0) return MHC_OK;
+  if (!x || !out || !inv_rms) return fail(MHC_ERR_NULL, "mhc_head_fwd: required pointer is NULL");
+  MHC_TRY(check_elem_align(x, x_dtype, "x"));
+  MHC_TRY(check_elem_align(out, x_dtype, "out"));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n == 1) return cuda_status(launch_head1_fwd(x_dtype, x, out, inv_rms, T, C, rms_eps, s), "mhc_head_fwd");
+  if (!phi || !alpha || !bias || !mix_raw) return fail(MHC_ERR_NULL, "mhc_head_fwd: phi/alpha/bias/mix_raw NULL");
+  const size_t need = mhc_head_fwd_workspace(T, n, C);
+  if (!workspace || workspace_bytes < need)
+    return fail(MHC_ERR_WORKSPACE, "mhc_head_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  CoefParams p{alpha, bias, nullptr, nullptr, nullptr, nullptr, param_dtype, 1.f, pre_eps, rms_eps, 0.f, 0, 0};
+  float *gate = reinterpret_cast<float *>(workspace);
+  MHC_TRY(cuda_status(launch_coef_fwd(2, n, x_dtype, x, T, C, phi, p, nullptr, nullptr, nullptr,
+                                      MHC_F32, inv_rms, mix_raw, gate, device_sm_count(), s),
+                      "mhc_head_fwd coef"));
+  return cuda_status(launch_aggregate(n, x_dtype, x, gate, out, T, C, s), "mhc_head_fwd aggregate");
+}
+
+size_t mhc_head_bwd_workspace(int64_t T, int n, int C) {
+  if (T < 0 || !n_ok(n) || C < 1) return 0;
+  if (n == 1) return 256;
+  return plan_pre_bwd(2, n, T, C, 0, device_sm_count()).total;
+}
+
+int mhc_head_bwd(const void *x, int x_dtype, int64_t T, int n, int C, const void *phi,
+                 const void *alpha, const void *bias, int param_dtype, float pre_eps, float rms_eps,
+                 const float *inv_rms, const float *mix_raw, const void *dout, void *dx, void *dphi,
+                 void *dalpha, void *dbias, void *workspace, size_t workspace_bytes, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(x_dtype) || !dtype_ok(param_dtype)) return fail(MHC_ERR_DTYPE, "mhc_head_bwd: bad dtype");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n == 1) {
+    if (T == 0) return MHC_OK;
+    if (!x || !inv_rms || !dout || !dx) return fail(MHC_ERR_NULL, "mhc_head_bwd: required pointer is NULL");
+    return cuda_status(launch_head1_bwd(x_dtype, x, inv_rms, dout, dx, T, C, s), "mhc_head_bwd");
+  }
+  if (T > 0 && (!alpha || !bias)) return fail(MHC_ERR_NULL, "mhc_head_bwd: alpha/bias NULL");
+  CoefParams p{alpha, bias, nullptr, nullptr, nullptr, nullptr, param_dtype, 1.f, pre_eps, rms_eps, 0.f, 0, 0};
+  return pre_bwd_common(2, x, x_dtype, T, n, C, phi, p, inv_rms, mix_raw, dout, nullptr, nullptr,
+                        nullptr, MHC_F32, nullptr, dx, dphi, dalpha, dbias, nullptr, nullptr, nullptr,
+                        nullptr, workspace, workspace_bytes, stream, "mhc_head_bwd");
+}
+
+int mhc_stream_expand_fwd(const void *x, void *out, int dtype, int64_t T, int n, int C, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(dtype)) return fail(MHC_ERR_DTYPE, "mhc_stream_expand_fwd: bad dtype");
+  if (T == 0) return MHC_OK;
+  if (!x || !out) return fail(MHC_ERR_NULL, "mhc_stream_expand_fwd: NULL pointer");
+  return cuda_status(launch_expand_fwd(dtype, x, out, T, n, C, reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_stream_expand_fwd");
+}
+
+int mhc_stream_expand_bwd(const void *dout, void *dx, int dtype, int64_t T, int n, int C, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  if (!dtype_ok(dtype)) return fail(MHC_ERR_DTYPE, "mhc_stream_expand_bwd: bad dtype");
+  if (T == 0) return MHC_OK;
+  if (!dout || !dx) return fail(MHC_ERR_NULL, "mhc_stream_expand_bwd: NULL pointer");
+  return cuda_status(launch_expand_bwd(dtype, dout, dx, T, n, C, reinterpret_cast<cudaStream_t>(stream)),
+                     "mhc_stream_expand_bwd");
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// Host-side launchers implemented by the kernel translation units and called by
+// the C ABI layer (mhc_capi.cu).  Arguments are validated by the caller; these
+// functions only pick the template instance and launch on `stream`.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mhc {
+
+struct CoefParams {
+  const void *alpha_pre, *bias_pre, *alpha_post, *bias_post, *alpha_res, *bias_res;
+  int param_dtype;
+  float post_mult, pre_eps, rms_eps, sk_eps;
+  int apply_sinkhorn, sk_iters;
+};
+
+// ---- forward --------------------------------------------------------------
+// mode: 0 FULL, 1 NOHRES, 2 HEAD.  `gate_ws` receives the fp32 aggregation
+// weights (h_pre, or the head weights), T x n.
+cudaError_t launch_coef_fwd(int mode, int n, int x_dtype, const void *x, int64_t T, int C,
+                            const void *phi, const CoefParams &p, void *h_pre, void *h_post,
+                            void *h_res, int coef_dtype, float *inv_rms, float *mixes,
+                            float *gate_ws, int sm_count, cudaStream_t stream);
+
+cudaError_t launch_aggregate(int n, int x_dtype, const void *x, const float *w, void *z,
+                             int64_t T, int C, cudaStream_t stream);
+
+cudaError_t launch_head1_fwd(int x_dtype, const void *x, void *out, float *inv_rms, int64_t T,
+                             int C, float rms_eps, cudaStream_t stream);
+cudaError_t launch_head1_bwd(int x_dtype, const void *x, const float *inv_rms, const void *dout,
+                             void *dx, int64_t T, int C, cudaStream_t stream);
+
+cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res, int h_res_dtype,
+                            const void *h_post, int h_post_dtype, const void *f, int f_dtype,
+                            void *out, int64_t T, int C, cudaStream_t stream);
+
+cudaError_t launch_post_bwd(int n, int x_dtype, const void *dout, const void *x, const void *h_res,
+                            int h_res_dtype, const void *h_post, int h_post_dtype, const void *f,
+                            int f_dtype, void *dx, void *dh_res, void *dh_post, void *df,
+                            int64_t T, int C, cudaStream_t stream);
+
+// ---- backward of the coefficient / aggregate stage --------------------------
+struct PreBwdPlan {
+  int fd;            // projection width
+  int k1_tokens;     // tokens per block of the coefficient-backward kernel
+  int k1_blocks;     // blocks of that kernel
+  int k2_kc;         // k columns per block of the dx / dphi kernel
+  int k2_kblocks;    // ceil(nC / kc)
+  int k2_tsplits;    // token splits (one dphi partial per split)
+  size_t off_dm, off_rowb, off_gate, off_dphi_part, off_coef_part, total;
+};
+
+PreBwdPlan plan_pre_bwd(int mode, int n, int64_t T, int C, int sk_iters, int sm_count);
+
+cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t T, int C,
+                           const void *phi, const CoefParams &p, const float *inv_rms,
+                           const float *mixes, const void *dz, const void *dh_pre,
+                           const void *dh_post, const void *dh_res, int coef_dtype,
+                           const void *dx_add, void *dx, void *dphi, void *dalpha_pre,
+                           void *dbias_pre, void *dalpha_post, void *dbias_post,
+                           void *dalpha_res, void *dbias_res, void *workspace,
+                           const PreBwdPlan &plan, cudaStream_t stream);
+
+// ---- stand-alone pieces -----------------------------------------------------
+cudaError_t launch_sinkhorn_fwd(int n, const void *M, int m_dtype, void *Y, int y_dtype,
+                                int64_t batch, int iters, float eps, cudaStream_t stream);
+cudaError_t launch_sinkhorn_bwd(int n, const void *M, int m_dtype, const void *dY, int dy_dtype,
+                                void *dM, int dm_dtype, int64_t batch, int iters, float eps,
+                                cudaStream_t stream);
+size_t sinkhorn_bwd_smem_per_item(int n, int iters);
+
+cudaError_t launch_expand_fwd(int dtype, const void *x, void *out, int64_t T, int n, int C,
+                              cudaStream_t stream);
+cudaError_t launch_expand_bwd(int dtype, const void *dout, void *dx, int64_t T, int n, int C,
+                              cudaStream_t stream);
+
+}  // namespace mhc

@@ -1,0 +1,149 @@
+// Stand-alone Sinkhorn-Knopp (forward and backward-by-recompute, one thread per
+// matrix) and the StreamExpand copy / its reduction.
+#include "mhc_device.cuh"
+#include "mhc_dispatch.cuh"
+#include "mhc_kernels.h"
+
+namespace mhc {
+
+template <int N>
+__global__ void __launch_bounds__(128)
+sinkhorn_fwd_kernel(const void *__restrict__ M, int mdt, void *__restrict__ Y, int ydt,
+                    int64_t batch, int iters, float eps) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float p[N * N];
+MHC_UNROLL_N
+  for (int k = 0; k < N * N; ++k) p[k] = load_dyn(M, mdt, b * N * N + k);
+  sinkhorn_fwd<N>(p, iters, eps);
+MHC_UNROLL_N
+  for (int k = 0; k < N * N; ++k) store_dyn(Y, ydt, b * N * N + k, p[k]);
+}
+
+template <int N>
+__global__ void __launch_bounds__(128)
+sinkhorn_bwd_kernel(const void *__restrict__ M, int mdt, const void *__restrict__ dY, int gdt,
+                    void *__restrict__ dM, int dmdt, int64_t batch, int iters, float eps, int TB) {
+  extern __shared__ float traj[];  // [steps][N*N][TB]
+  const int t = threadIdx.x;
+  const int64_t b = (int64_t)blockIdx.x * TB + t;
+  if (t >= TB || b >= batch) return;
+  float m[N * N], g[N * N];
+MHC_UNROLL_N
+  for (int k = 0; k < N * N; ++k) {
+    m[k] = load_dyn(M, mdt, b * N * N + k);
+    g[k] = load_dyn(dY, gdt, b * N * N + k);
+  }
+  sinkhorn_bwd<N>(m, g, iters, eps, traj + t, TB);
+MHC_UNROLL_N
+  for (int k = 0; k < N * N; ++k) store_dyn(dM, dmdt, b * N * N + k, g[k]);
+}
+
+size_t sinkhorn_bwd_smem_per_item(int n, int iters) {
+  const int steps = iters < 1 ? 1 : iters;
+  return (size_t)steps * n * n * 4;
+}
+
+cudaError_t launch_sinkhorn_fwd(int n, const void *M, int m_dtype, void *Y, int y_dtype,
+                                int64_t batch, int iters, float eps, cudaStream_t stream) {
+  if (batch == 0) return cudaSuccess;
+  return with_n(n, [&](auto nn) {
+    constexpr int N = decltype(nn)::value;
+    const unsigned grid = (unsigned)((batch + 127) / 128);
+    sinkhorn_fwd_kernel<N><<<grid, 128, 0, stream>>>(M, m_dtype, Y, y_dtype, batch, iters, eps);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_sinkhorn_bwd(int n, const void *M, int m_dtype, const void *dY, int dy_dtype,
+                                void *dM, int dm_dtype, int64_t batch, int iters, float eps,
+                                cudaStream_t stream) {
+  if (batch == 0) return cudaSuccess;
+  const size_t per = sinkhorn_bwd_smem_per_item(n, iters);
+  int TB = (int)((96 * 1024) / per);
+  if (TB > 128) TB = 128;
+  if (TB < 1) TB = 1;
+  const size_t smem = per * TB;
+  return with_n(n, [&](auto nn) {
+    constexpr int N = decltype(nn)::value;
+    auto kern = sinkhorn_bwd_kernel<N>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const unsigned grid = (unsigned)((batch + TB - 1) / TB);
+    kern<<<grid, 128, smem, stream>>>(M, m_dtype, dY, dy_dtype, dM, dm_dtype, batch, iters, eps, TB);
+    return cudaGetLastError();
+  });
+}
+
+// out[t, i*C + c] = x[t, c]
+template <typename T>
+__global__ void __launch_bounds__(256)
+expand_fwd_kernel(const T *__restrict__ x, T *__restrict__ out, int64_t T_, int n, int C, bool vec) {
+  const int64_t nC = (int64_t)n * C;
+  if (vec) {
+    constexpr int VEC = 16 / sizeof(T);
+    const int vpt = C / VEC;
+    const int64_t items = T_ * vpt;
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+         it += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = it / vpt;
+      const int v = (int)(it - t * vpt);
+      const uint4 r = ldg_stream(x + t * C + (int64_t)v * VEC);
+      for (int i = 0; i < n; ++i) stg_stream(out + t * nC + (int64_t)i * C + (int64_t)v * VEC, r);
+    }
+  } else {
+    const int64_t items = T_ * C;
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+         it += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = it / C;
+      const int c = (int)(it - t * C);
+      const T v = x[it];
+      for (int i = 0; i < n; ++i) out[t * nC + (int64_t)i * C + c] = v;
+    }
+  }
+}
+
+// dx[t, c] = sum_i dout[t, i*C + c]
+template <typename T>
+__global__ void __launch_bounds__(256)
+expand_bwd_kernel(const T *__restrict__ dout, T *__restrict__ dx, int64_t T_, int n, int C) {
+  const int64_t nC = (int64_t)n * C;
+  const int64_t items = T_ * C;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = it / C;
+    const int c = (int)(it - t * C);
+    float a = 0.f;
+    for (int i = 0; i < n; ++i) a += to_f(dout[t * nC + (int64_t)i * C + c]);
+    dx[it] = from_f<T>(a);
+  }
+}
+
+cudaError_t launch_expand_fwd(int dtype, const void *x, void *out, int64_t T, int n, int C,
+                              cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int sms = device_sm_count();
+  return with_dtype(dtype, [&](auto tag) {
+    using Tx = decltype(tag);
+    constexpr int VEC = 16 / sizeof(Tx);
+    const bool vec = C % VEC == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0;
+    const int64_t items = T * (vec ? C / VEC : C);
+    expand_fwd_kernel<Tx><<<grid_for(items, 256, sms, 16), 256, 0, stream>>>(
+        (const Tx *)x, (Tx *)out, T, n, C, vec);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_expand_bwd(int dtype, const void *dout, void *dx, int64_t T, int n, int C,
+                              cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int sms = device_sm_count();
+  return with_dtype(dtype, [&](auto tag) {
+    using Tx = decltype(tag);
+    expand_bwd_kernel<Tx><<<grid_for(T * C, 256, sms, 16), 256, 0, stream>>>(
+        (const Tx *)dout, (Tx *)dx, T, n, C);
+    return cudaGetLastError();
+  });
+}
+
+}  // namespace mhc

@@ -1,0 +1,442 @@
+// Backward of the coefficient stage + pre-aggregate (generic CUDA-core path).
+//
+// Three launches, no atomics (deterministic):
+//  K1 coef_bwd_kernel  : per token, the dot products <dz, x_i> (one warp per
+//     token), then one thread per token runs the gate / Sinkhorn backward (the
+//     Sinkhorn trajectory is recomputed into shared memory) and writes dm =
+//     dL/dmixes, the RMS-backward row coefficient and the aggregation weights.
+//     Per-block sums of the alpha / bias gradients go to the workspace.
+//  K2 dx_dphi_kernel   : grid (k-chunks x token splits).  For its k-chunk a block
+//     keeps phi^T in shared memory and, per 32-token tile,
+//       dx = inv*(dm @ phi^T) - rowb*x + w_i*dz + dx_add
+//     and accumulates dphi[k, :] += (x*inv)[t,k] * dm[t,:] in registers.
+//  K3 reduce kernels   : fixed-order sums of the per-split dphi partials and of
+//     the per-block alpha / bias partials.
+#include "mhc_device.cuh"
+#include "mhc_dispatch.cuh"
+#include "mhc_kernels.h"
+
+namespace mhc {
+
+static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static inline int fd_of(int mode, int n) {
+  return mode == FULL ? 2 * n + n * n : (mode == NOHRES ? 2 * n : n);
+}
+
+// number of per-block coefficient partials: 3 alphas + FD biases
+static inline int ng_of(int mode, int n) { return 3 + fd_of(mode, n); }
+
+static inline int k2_kc_of(int fd) { return fd <= 96 ? 64 : 16; }
+
+PreBwdPlan plan_pre_bwd(int mode, int n, int64_t T, int C, int sk_iters, int sm_count) {
+  PreBwdPlan p{};
+  p.fd = fd_of(mode, n);
+  const int64_t nC = (int64_t)n * C;
+  int tokens = 32;
+  if (mode == FULL) {
+    const int steps = sk_iters < 1 ? 1 : sk_iters;
+    const size_t per = (size_t)steps * n * n * 4;
+    const size_t budget = 96 * 1024;
+    int t = (int)(budget / per);
+    if (t < 1) t = (per <= 200 * 1024) ? 1 : 0;  // 0 => unsupported
+    if (t < tokens) tokens = t;
+  }
+  p.k1_tokens = tokens;
+  p.k1_blocks = tokens > 0 ? (int)((T + tokens - 1) / tokens) : 0;
+  p.k2_kc = k2_kc_of(p.fd);
+  p.k2_kblocks = (int)((nC + p.k2_kc - 1) / p.k2_kc);
+  const int64_t tiles = (T + 31) / 32;
+  int64_t target = (int64_t)(sm_count > 0 ? sm_count : 148) * 8 / (p.k2_kblocks > 0 ? p.k2_kblocks : 1);
+  if (target < 1) target = 1;
+  if (target > tiles) target = tiles;
+  if (target > 64) target = 64;
+  if (target < 1) target = 1;
+  p.k2_tsplits = (int)target;
+  size_t off = 0;
+  p.off_dm = off;        off = align256(off + (size_t)T * p.fd * 4);
+  p.off_rowb = off;      off = align256(off + (size_t)T * 4);
+  p.off_gate = off;      off = align256(off + (size_t)T * n * 4);
+  p.off_dphi_part = off; off = align256(off + (size_t)p.k2_tsplits * nC * p.fd * 4);
+  p.off_coef_part = off; off = align256(off + (size_t)(p.k1_blocks > 0 ? p.k1_blocks : 1) * ng_of(mode, n) * 4);
+  p.total = off;
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// K1
+// ---------------------------------------------------------------------------
+template <int N, int MODE, typename Tx>
+__global__ void __launch_bounds__(256)
+coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
+                const float *__restrict__ inv_rms, const float *__restrict__ mixes,
+                const Tx *__restrict__ dz, const void *dh_pre, const void *dh_post,
+                const void *dh_res, int coef_dtype, int TB,
+                float *__restrict__ dm_ws, float *__restrict__ rowb_ws, float *__restrict__ gate_ws,
+                float *__restrict__ coef_part, bool vecok) {
+  constexpr int FD = Dims<N, MODE>::FD;
+  constexpr int NG = 3 + FD;
+  constexpr int NPAR = 3 + 2 * N + N * N;
+  constexpr int VEC = 16 / sizeof(Tx);
+  extern __shared__ float4 smem4[];
+  float *smem = reinterpret_cast<float *>(smem4);
+  float *par = smem;                     // [NPAR]
+  float *dots = par + NPAR;              // [TB][N]
+  float *pg = dots + TB * N;             // [TB][NG]
+  float *traj = pg + TB * NG;            // [steps][N*N][TB]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t tok0 = (int64_t)blockIdx.x * TB;
+  const int64_t nC = (int64_t)N * C;
+  for (int i = tid; i < NPAR; i += blockDim.x) {
+    float v = 0.f;
+    const int dt = p.param_dtype;
+    if (i == 0) v = load_dyn(p.alpha_pre, dt, 0);
+    else if (i == 1) { if (MODE != HEAD) v = load_dyn(p.alpha_post, dt, 0); }
+    else if (i == 2) { if (MODE == FULL) v = load_dyn(p.alpha_res, dt, 0); }
+    else if (i < 3 + N) v = load_dyn(p.bias_pre, dt, i - 3);
+    else if (i < 3 + 2 * N) { if (MODE != HEAD) v = load_dyn(p.bias_post, dt, i - 3 - N); }
+    else { if (MODE == FULL) v = load_dyn(p.bias_res, dt, i - 3 - 2 * N); }
+    par[i] = v;
+  }
+
+  // phase 1: <dz, x_i> per token, one warp per token
+  const int vpt = vecok ? C / VEC : C;
+  for (int t = warp; t < TB; t += (blockDim.x >> 5)) {
+    const int64_t tok = tok0 + t;
+    float d[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = 0.f;
+    if (tok < T) {
+      const Tx *xr = x + tok * nC;
+      const Tx *gr = dz + tok * C;
+      for (int v = lane; v < vpt; v += 32) {
+        const int64_t off = vecok ? (int64_t)v * VEC : v;
+        if (vecok) {
+          Pack<Tx> pgz;
+          pgz.raw = ldg_keep(gr + off);
+          float g[VEC];
+          pgz.to_float(g);
+#pragma unroll
+          for (int i = 0; i < N; ++i) {
+            Pack<Tx> px;
+            px.raw = ldg_keep(xr + (int64_t)i * C + off);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) d[i] = fmaf(g[e], px.get(e), d[i]);
+          }
+        } else {
+          const float g = to_f(gr[off]);
+#pragma unroll
+          for (int i = 0; i < N; ++i) d[i] = fmaf(g, to_f(xr[(int64_t)i * C + off]), d[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = warp_sum(d[i]);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) dots[t * N + i] = d[i];
+    }
+  }
+  __syncthreads();
+
+  // phase 2: one thread per token
+  for (int t = tid; t < TB; t += blockDim.x) {
+    const int64_t tok = tok0 + t;
+    float *g_out = pg + t * NG;
+    for (int k = 0; k < NG; ++k) g_out[k] = 0.f;
+    if (tok >= T) continue;
+    float m[FD], dm[FD];
+    MHC_UNROLL_N
+    for (int j = 0; j < FD; ++j) {
+      m[j] = mixes[tok * FD + j];
+      dm[j] = 0.f;
+    }
+    const float inv = inv_rms[tok];
+    if constexpr (MODE == HEAD) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float s = sigmoidf_(__fadd_rn(__fmul_rn(m[i], par[0]), par[3 + i]));
+        gate_ws[tok * N + i] = s + p.pre_eps;
+        const float da = dots[t * N + i] * s * (1.f - s);
+        dm[i] = par[0] * da;
+        g_out[0] += da * m[i];
+        g_out[3 + i] = da;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float sp = sigmoidf_(__fadd_rn(__fmul_rn(m[i], par[0]), par[3 + i]));
+        gate_ws[tok * N + i] = sp + p.pre_eps;
+        float gp = dots[t * N + i];
+        if (dh_pre) gp += load_dyn(dh_pre, coef_dtype, tok * N + i);
+        const float dpre = gp * sp * (1.f - sp);
+        dm[i] = par[0] * dpre;
+        g_out[0] += dpre * m[i];
+        g_out[3 + i] = dpre;
+        const float so = sigmoidf_(__fadd_rn(__fmul_rn(m[N + i], par[1]), par[3 + N + i]));
+        const float go = dh_post ? load_dyn(dh_post, coef_dtype, tok * N + i) : 0.f;
+        const float dpost = go * so * (1.f - so) * p.post_mult;
+        dm[N + i] = par[1] * dpost;
+        g_out[1] += dpost * m[N + i];
+        g_out[3 + N + i] = dpost;
+      }
+      if constexpr (MODE == FULL) {
+        float gl[N * N];
+        MHC_UNROLL_N
+        for (int k = 0; k < N * N; ++k) gl[k] = dh_res ? load_dyn(dh_res, coef_dtype, tok * (N * N) + k) : 0.f;
+        if (p.apply_sinkhorn && dh_res) {
+          float L[N * N];
+          MHC_UNROLL_N
+          for (int k = 0; k < N * N; ++k) L[k] = __fadd_rn(__fmul_rn(m[2 * N + k], par[2]), par[3 + 2 * N + k]);
+          sinkhorn_bwd<N>(L, gl, p.sk_iters, p.sk_eps, traj + t, TB);
+        }
+        MHC_UNROLL_N
+        for (int k = 0; k < N * N; ++k) {
+          dm[2 * N + k] = par[2] * gl[k];
+          g_out[2] += gl[k] * m[2 * N + k];
+          g_out[3 + 2 * N + k] = gl[k];
+        }
+      }
+    }
+    float s = 0.f;
+    MHC_UNROLL_N
+    for (int j = 0; j < FD; ++j) {
+      s = fmaf(dm[j], m[j], s);
+      dm_ws[tok * FD + j] = dm[j];
+    }
+    rowb_ws[tok] = inv * inv * s / (float)nC;
+  }
+  __syncthreads();
+  // phase 3: fixed-order per-block sums of the coefficient gradients
+  for (int k = tid; k < NG; k += blockDim.x) {
+    float a = 0.f;
+    for (int t = 0; t < TB; ++t) a += pg[t * NG + k];
+    coef_part[(int64_t)blockIdx.x * NG + k] = a;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K2
+// ---------------------------------------------------------------------------
+template <int N, int MODE, typename Tx>
+__global__ void __launch_bounds__(256)
+dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restrict__ phi, int pdt,
+               const float *__restrict__ inv_rms, const float *__restrict__ dm_ws,
+               const float *__restrict__ rowb_ws, const float *__restrict__ gate_ws,
+               const Tx *__restrict__ dz, const Tx *__restrict__ dx_add, Tx *__restrict__ dx,
+               float *__restrict__ dphi_part, int tsplits) {
+  constexpr int FD = Dims<N, MODE>::FD;
+  constexpr int KC = FD <= 96 ? 64 : 16;
+  constexpr int JGRP = 256 / KC;               // j groups (dphi) / token rows (dx)
+  constexpr int RJ = (FD + JGRP - 1) / JGRP;
+  constexpr int TT = 32;                       // tokens per tile
+  constexpr int RR = TT / JGRP;                // dx rows per thread
+  constexpr int XSW = KC + 1;
+  extern __shared__ float4 smem4[];
+  float *smem = reinterpret_cast<float *>(smem4);
+  float *psT = smem;                  // [FD][KC]
+  float *xs = psT + FD * KC;          // [TT][XSW]
+  float *dms = xs + TT * XSW;         // [TT][FD]
+  float *tinv = dms + TT * FD;        // [TT]
+  float *trow = tinv + TT;            // [TT]
+  float *tgate = trow + TT;           // [TT][N]
+
+  const int tid = threadIdx.x;
+  const int kk = tid % KC, jgrp = tid / KC;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t k0 = (int64_t)blockIdx.x * KC;
+  const int64_t kglob = k0 + kk;
+  const bool kvalid = kglob < nC;
+  const int stream_i = kvalid ? (int)(kglob / C) : 0;
+  const int cc = kvalid ? (int)(kglob - (int64_t)stream_i * C) : 0;
+
+  for (int e = tid; e < KC * FD; e += blockDim.x) {
+    const int r = e / FD, j = e - r * FD;
+    float v = 0.f;
+    if (k0 + r < nC) v = load_dyn(phi, pdt, (k0 + r) * FD + j);
+    psT[j * KC + r] = v;
+  }
+
+  // token range of this split
+  const int64_t tiles = (T + TT - 1) / TT;
+  const int64_t tiles_per = (tiles + tsplits - 1) / tsplits;
+  const int64_t tile_beg = (int64_t)blockIdx.y * tiles_per;
+  int64_t tile_end = tile_beg + tiles_per;
+  if (tile_end > tiles) tile_end = tiles;
+
+  float acc[RJ];
+#pragma unroll
+  for (int q = 0; q < RJ; ++q) acc[q] = 0.f;
+
+  for (int64_t tile = tile_beg; tile < tile_end; ++tile) {
+    const int64_t t0 = tile * TT;
+    __syncthreads();
+    for (int e = tid; e < TT * KC; e += blockDim.x) {
+      const int r = e / KC, c = e - r * KC;
+      const int64_t tok = t0 + r;
+      float v = 0.f;
+      if (tok < T && k0 + c < nC) v = to_f(x[tok * nC + k0 + c]);
+      xs[r * XSW + c] = v;
+    }
+    for (int e = tid; e < TT * FD; e += blockDim.x) {
+      const int r = e / FD;
+      const int64_t tok = t0 + r;
+      dms[e] = tok < T ? dm_ws[t0 * FD + e] : 0.f;
+    }
+    for (int e = tid; e < TT; e += blockDim.x) {
+      const int64_t tok = t0 + e;
+      tinv[e] = tok < T ? inv_rms[tok] : 0.f;
+      trow[e] = tok < T ? rowb_ws[tok] : 0.f;
+    }
+    for (int e = tid; e < TT * N; e += blockDim.x) {
+      const int64_t tok = t0 + e / N;
+      tgate[e] = tok < T ? gate_ws[t0 * N + e] : 0.f;
+    }
+    __syncthreads();
+    // dx for rows jgrp + JGRP*r, column kk
+    if (kvalid) {
+#pragma unroll
+      for (int r = 0; r < RR; ++r) {
+        const int row = jgrp + JGRP * r;
+        const int64_t tok = t0 + row;
+        if (tok >= T) continue;
+        float a = 0.f;
+#pragma unroll 8
+        for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
+        float v = tinv[row] * a - trow[row] * xs[row * XSW + kk];
+        v = fmaf(tgate[row * N + stream_i], to_f(dz[tok * C + cc]), v);
+        if (dx_add) v += to_f(dx_add[tok * nC + kglob]);
+        dx[tok * nC + kglob] = from_f<Tx>(v);
+      }
+    }
+    // dphi[k, j] += sum_t (x * inv)[t, k] * dm[t, j]
+#pragma unroll 4
+    for (int t = 0; t < TT; ++t) {
+      const float xn = xs[t * XSW + kk] * tinv[t];
+#pragma unroll
+      for (int q = 0; q < RJ; ++q) {
+        const int j = jgrp + JGRP * q;
+        if (j < FD) acc[q] = fmaf(xn, dms[t * FD + j], acc[q]);
+      }
+    }
+  }
+  if (kvalid) {
+    float *dst = dphi_part + ((int64_t)blockIdx.y * nC + kglob) * FD;
+#pragma unroll
+    for (int q = 0; q < RJ; ++q) {
+      const int j = jgrp + JGRP * q;
+      if (j < FD) dst[j] = acc[q];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K3
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+reduce_dphi_kernel(const float *__restrict__ part, int splits, int64_t elems, void *dphi, int pdt) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < elems;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float a = 0.f;
+    for (int s = 0; s < splits; ++s) a += part[(int64_t)s * elems + e];
+    store_dyn(dphi, pdt, e, a);
+  }
+}
+
+// one warp per coefficient-gradient slot; lane-strided fixed-order sums then a
+// fixed butterfly
+__global__ void __launch_bounds__(256)
+reduce_coef_kernel(const float *__restrict__ part, int blocks, int ng, int n, int mode, int pdt,
+                   void *da_pre, void *db_pre, void *da_post, void *db_post, void *da_res,
+                   void *db_res) {
+  const int lane = threadIdx.x & 31;
+  const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (g >= ng) return;
+  float a = 0.f;
+  for (int b = lane; b < blocks; b += 32) a += part[(int64_t)b * ng + g];
+  a = warp_sum(a);
+  if (lane != 0) return;
+  if (g == 0) { if (da_pre) store_dyn(da_pre, pdt, 0, a); return; }
+  if (g == 1) { if (da_post && mode != HEAD) store_dyn(da_post, pdt, 0, a); return; }
+  if (g == 2) { if (da_res && mode == FULL) store_dyn(da_res, pdt, 0, a); return; }
+  const int j = g - 3;
+  if (j < n) { if (db_pre) store_dyn(db_pre, pdt, j, a); return; }
+  if (mode == HEAD) return;
+  if (j < 2 * n) { if (db_post) store_dyn(db_post, pdt, j - n, a); return; }
+  if (mode == FULL && db_res) store_dyn(db_res, pdt, j - 2 * n, a);
+}
+
+cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t T, int C,
+                           const void *phi, const CoefParams &p, const float *inv_rms,
+                           const float *mixes, const void *dz, const void *dh_pre,
+                           const void *dh_post, const void *dh_res, int coef_dtype,
+                           const void *dx_add, void *dx, void *dphi, void *dalpha_pre,
+                           void *dbias_pre, void *dalpha_post, void *dbias_post,
+                           void *dalpha_res, void *dbias_res, void *workspace,
+                           const PreBwdPlan &plan, cudaStream_t stream) {
+  char *ws = reinterpret_cast<char *>(workspace);
+  float *dm_ws = reinterpret_cast<float *>(ws + plan.off_dm);
+  float *rowb_ws = reinterpret_cast<float *>(ws + plan.off_rowb);
+  float *gate_ws = reinterpret_cast<float *>(ws + plan.off_gate);
+  float *dphi_part = reinterpret_cast<float *>(ws + plan.off_dphi_part);
+  float *coef_part = reinterpret_cast<float *>(ws + plan.off_coef_part);
+  const int64_t nC = (int64_t)n * C;
+  const int sms = device_sm_count();
+  return with_mode(mode, [&](auto md) {
+    constexpr int MODE = decltype(md)::value;
+    return with_n(n, [&](auto nn) {
+      constexpr int N = decltype(nn)::value;
+      return with_dtype(x_dtype, [&](auto tag) -> cudaError_t {
+        using Tx = decltype(tag);
+        constexpr int FD = Dims<N, MODE>::FD;
+        constexpr int NG = 3 + FD;
+        constexpr int VEC = 16 / sizeof(Tx);
+        if (T > 0) {
+          // K1
+          const int TB = plan.k1_tokens;
+          const int steps = p.sk_iters < 1 ? 1 : p.sk_iters;
+          const size_t traj = (MODE == FULL && p.apply_sinkhorn) ? (size_t)steps * N * N * TB : 0;
+          const size_t smem1 = ((size_t)(3 + 2 * N + N * N) + (size_t)TB * N + (size_t)TB * NG + traj) * 4;
+          const bool vecok = C % VEC == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)dz & 15) == 0;
+          auto k1 = coef_bwd_kernel<N, MODE, Tx>;
+          cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+          if (e != cudaSuccess) return e;
+          k1<<<plan.k1_blocks, 256, smem1, stream>>>((const Tx *)x, T, C, p, inv_rms, mixes,
+                                                     (const Tx *)dz, dh_pre, dh_post, dh_res,
+                                                     coef_dtype, TB, dm_ws, rowb_ws, gate_ws, coef_part,
+                                                     vecok);
+          if ((e = cudaGetLastError()) != cudaSuccess) return e;
+          // K2
+          constexpr int KC = FD <= 96 ? 64 : 16;
+          const size_t smem2 = ((size_t)FD * KC + 32 * (KC + 1) + 32 * FD + 64 + 32 * N) * 4;
+          auto k2 = dx_dphi_kernel<N, MODE, Tx>;
+          e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+          if (e != cudaSuccess) return e;
+          dim3 grid2(plan.k2_kblocks, plan.k2_tsplits);
+          k2<<<grid2, 256, smem2, stream>>>((const Tx *)x, T, C, phi, p.param_dtype, inv_rms, dm_ws,
+                                            rowb_ws, gate_ws, (const Tx *)dz, (const Tx *)dx_add,
+                                            (Tx *)dx, dphi_part, plan.k2_tsplits);
+          if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+        // K3
+        const int64_t elems = nC * FD;
+        if (dphi) {
+          if (T > 0) {
+            reduce_dphi_kernel<<<grid_for(elems, 256, sms, 4), 256, 0, stream>>>(
+                dphi_part, plan.k2_tsplits, elems, dphi, p.param_dtype);
+          } else {
+            reduce_dphi_kernel<<<grid_for(elems, 256, sms, 4), 256, 0, stream>>>(
+                dphi_part, 0, elems, dphi, p.param_dtype);
+          }
+        }
+        reduce_coef_kernel<<<(NG + 7) / 8, 256, 0, stream>>>(
+            coef_part, T > 0 ? plan.k1_blocks : 0, NG, N, MODE, p.param_dtype, dalpha_pre,
+            dbias_pre, dalpha_post, dbias_post, dalpha_res, dbias_res);
+        return cudaGetLastError();
+      });
+    });
+  });
+}
+
+}  // namespace mhc

@@ -1,0 +1,120 @@
+"""ctypes binding of ``libmhc_b200.so`` (the C ABI in ``include/mhc_b200.h``).
+
+This is the only place Python touches the native library.  Every call passes
+raw device pointers, sizes, dtype codes and the current CUDA stream; a
+non-zero status raises ``RuntimeError`` with the library's message.  There is
+no CPU path: a CPU tensor, a missing library or a CUDA-less process is an
+error, raised before anything is launched.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("MHC_B200_LIB") or os.path.join(_HERE, "libmhc_b200.so")
+
+F32, BF16, F16 = 0, 1, 2
+_DTYPE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes)
+_PROTOS = {
+    "mhc_abi_version": (_I, []),
+    "mhc_last_error": (ctypes.c_char_p, []),
+    "mhc_device_sm_count": (_I, []),
+    "mhc_pre_fwd_workspace": (_SZ, [_I64, _I, _I, _I]),
+    "mhc_pre_fwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
+                         _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),
+    "mhc_post_fwd": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _I64, _I, _I, _P]),
+    "mhc_post_bwd": (_I, [_P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _I64, _I, _I, _P]),
+    "mhc_pre_bwd_workspace": (_SZ, [_I64, _I, _I, _I, _I, _I]),
+    "mhc_pre_bwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
+                         _F, _F, _F, _F, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                         _P, _P, _P, _P, _SZ, _P]),
+    "mhc_sinkhorn_fwd": (_I, [_P, _I, _P, _I, _I64, _I, _I, _F, _P]),
+    "mhc_sinkhorn_bwd": (_I, [_P, _I, _P, _I, _P, _I, _I64, _I, _I, _F, _P]),
+    "mhc_head_fwd_workspace": (_SZ, [_I64, _I, _I]),
+    "mhc_head_fwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _I, _F, _F, _P, _P, _P, _P, _SZ, _P]),
+    "mhc_head_bwd_workspace": (_SZ, [_I64, _I, _I]),
+    "mhc_head_bwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _I, _F, _F, _P, _P, _P, _P, _P, _P,
+                          _P, _P, _SZ, _P]),
+    "mhc_stream_expand_fwd": (_I, [_P, _P, _I, _I64, _I, _I, _P]),
+    "mhc_stream_expand_bwd": (_I, [_P, _P, _I, _I64, _I, _I, _P]),
+}
+
+EXPORTED = tuple(_PROTOS)
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: str | None = None):
+    """Load (once) and return the ctypes handle; raises if the file is missing."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise RuntimeError(
+                f"mHC native library not found at {p}; build it with "
+                f"`python minimind-mhc_b200/build.py` (there is no CPU fallback)")
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in _PROTOS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def lib():
+    return _lib if _lib is not None else load_library()
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DTYPE[t]
+    except KeyError:
+        raise TypeError(f"mHC kernels support float32/bfloat16/float16, got {t}") from None
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "mHC B200 kernels run on CUDA tensors only (this build has no CPU path); "
+                f"got a tensor on {t.device}")
+
+
+def check(status: int, what: str):
+    if status != 0:
+        msg = lib().mhc_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed with status {status}: {msg}")
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def call(name: str, *args):
+    check(getattr(lib(), name)(*args), name)

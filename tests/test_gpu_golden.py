@@ -1,0 +1,157 @@
+"""GPU parity against the reference's golden vectors (tests/golden/golden.pt).
+
+Every case runs the B200 kernels through the reference-API autograd Functions
+and modules (which call the C ABI) on the golden inputs and compares outputs
+and gradients with the reference's own outputs, using the reference
+self-tests' acceptance rule and tolerances (model/mhc_fused.py:871-876,
+:1089-1098; model/mhc_fused_no_hres.py:845-853), tightened for fp32.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _cuda(ts):
+    return [t.to(DEV) if t is not None else None for t in ts]
+
+
+def _mlp(w1, w2):
+    return lambda z: F.silu(z @ w1.t()) @ w2.t()
+
+
+def test_sinkhorn_golden(golden):
+    from model.mhc_fused import sinkhorn_normalize
+    for k in [k for k in golden if k.startswith("sinkhorn_")]:
+        g = golden[k]
+        m = g["M"].to(DEV).requires_grad_(True)
+        y = sinkhorn_normalize(m, g["iters"], g["eps"])
+        assert_close(k + ".Y", g["Y"], y, 2e-6, 2e-6)
+        (dm,) = torch.autograd.grad(y, m, g["dY"].to(DEV))
+        assert_close(k + ".dM", g["dM"], dm, 1e-5, 1e-4)
+
+
+def test_pre_phase_full_golden(golden):
+    from model.mhc_fused import _PrePhaseFullFn
+    for k in [k for k in golden if k.startswith("pre_full_")]:
+        g = golden[k]
+        f32 = g["x"].dtype == torch.float32
+        atol, rtol = (1e-4, 1e-4) if f32 else (1e-1, 1e-2)
+        leaves = [t.to(DEV).requires_grad_(True) for t in [g["x"]] + g["params"]]
+        z, hp, ho, hr = _PrePhaseFullFn.apply(*leaves, 2.0, 1e-6, 1e-6, g["n"], g["C"])
+        for name, a, b in [("z", g["z"], z), ("h_pre", g["h_pre"], hp), ("h_post", g["h_post"], ho),
+                           ("h_res_raw", g["h_res_raw"], hr)]:
+            assert_close(f"{k}.{name}", a, b, atol, rtol)
+        gr = torch.autograd.grad([z, ho, hr], leaves, _cuda([g["g_z"], g["g_h_post"], g["g_h_res_raw"]]))
+        for i, (a, b) in enumerate(zip(g["grads"], gr)):
+            mult = 5 if i == 1 else 1  # grad_W: the reference's x5 allowance
+            assert_close(f"{k}.grad{i}", a, b, atol * mult, rtol * mult)
+
+
+def test_post_phase_full_golden(golden):
+    from model.mhc_fused import _PostPhaseFullFn
+    for k in [k for k in golden if k.startswith("post_full_")]:
+        g = golden[k]
+        f32 = g["x"].dtype == torch.float32
+        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 5e-3)
+        leaves = [t.to(DEV).requires_grad_(True) for t in (g["x"], g["h_res"], g["h_post"], g["f"])]
+        o = _PostPhaseFullFn.apply(*leaves, g["n"], g["C"])
+        assert_close(k + ".out", g["out"], o, atol, rtol)
+        gr = torch.autograd.grad(o, leaves, g["g_out"].to(DEV))
+        for i, (a, b) in enumerate(zip(g["grads"], gr)):
+            mult = 5 if i == 1 else 1
+            assert_close(f"{k}.grad{i}", a, b, atol * mult, rtol * mult)
+
+
+def _module_case(g, mod, k):
+    f32 = g["x"].dtype == torch.float32
+    atol, rtol = (1e-4, 1e-4) if f32 else (2e-1, 2e-2)
+    mod = mod.to(DEV)
+    assert [n for n, _ in mod.named_parameters()] == list(g["param_names"])
+    with torch.no_grad():
+        for p, v in zip(mod.parameters(), g["params"]):
+            p.copy_(v.to(p.dtype))
+    x = g["x"].to(DEV).requires_grad_(True)
+    fn = _mlp(g["w1"].to(DEV), g["w2"].to(DEV)) if g["sub"] == "mlp" else (lambda z: z)
+    y = mod(x, fn)
+    assert_close(k + ".out", g["out"], y, atol, rtol)
+    loss = y.float().pow(2).mean()
+    ps = [p for _, p in mod.named_parameters()]
+    gr = torch.autograd.grad(loss, [x] + ps)
+    names = ["x"] + [n for n, _ in mod.named_parameters()]
+    for name, a, b in zip(names, g["grads"], gr):
+        mult = 1 if name == "x" else 5
+        assert_close(f"{k}.grad_{name}", a, b, atol * mult, rtol * mult)
+
+
+def test_full_module_golden(golden):
+    from model.mhc_fused import MHCConnection_Fused
+    for k in [k for k in golden if k.startswith("module_full_")]:
+        g = golden[k]
+        mod = MHCConnection_Fused(g["n"], g["C"], sinkhorn_iters=g["iters"]).to(g["x"].dtype)
+        _module_case(g, mod, k)
+
+
+def test_no_hres_golden(golden):
+    from model.mhc_fused_no_hres import MHCConnection_FusedNoHres, _PostPhaseFn, _PrePhaseFn
+    for k in [k for k in golden if k.startswith("pre_nohres_")]:
+        g = golden[k]
+        f32 = g["x"].dtype == torch.float32
+        atol, rtol = (1e-4, 1e-4) if f32 else (1e-1, 1e-2)
+        leaves = [t.to(DEV).requires_grad_(True) for t in [g["x"]] + g["params"]]
+        z, hp, ho = _PrePhaseFn.apply(*leaves, 2.0, 1e-6, 1e-6, g["n"], g["C"])
+        for name, a, b in [("z", g["z"], z), ("h_pre", g["h_pre"], hp), ("h_post", g["h_post"], ho)]:
+            assert_close(f"{k}.{name}", a, b, atol, rtol)
+        gr = torch.autograd.grad([z, ho], leaves, _cuda([g["g_z"], g["g_h_post"]]))
+        for i, (a, b) in enumerate(zip(g["grads"], gr)):
+            mult = 5 if i == 1 else 1
+            assert_close(f"{k}.grad{i}", a, b, atol * mult, rtol * mult)
+    for k in [k for k in golden if k.startswith("post_nohres_")]:
+        g = golden[k]
+        f32 = g["x"].dtype == torch.float32
+        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 5e-3)
+        leaves = [t.to(DEV).requires_grad_(True) for t in (g["x"], g["h_post"], g["f"])]
+        o = _PostPhaseFn.apply(*leaves, g["n"], g["C"])
+        assert_close(k + ".out", g["out"], o, atol, rtol)
+        gr = torch.autograd.grad(o, leaves, g["g_out"].to(DEV))
+        for i, (a, b) in enumerate(zip(g["grads"], gr)):
+            assert_close(f"{k}.grad{i}", a, b, atol, rtol)
+    for k in [k for k in golden if k.startswith("module_nohres_")]:
+        g = golden[k]
+        mod = MHCConnection_FusedNoHres(g["n"], g["C"]).to(g["x"].dtype)
+        _module_case(g, mod, k)
+
+
+def test_head_and_expand_golden(golden):
+    from model.mhc_common import MHCHead, StreamExpand
+    for k in [k for k in golden if k.startswith("head_")]:
+        g = golden[k]
+        f32 = g["x"].dtype == torch.float32
+        atol, rtol = (1e-4, 1e-4) if f32 else (1e-1, 1e-2)
+        mod = MHCHead(g["n"], g["C"]).to(g["x"].dtype).to(DEV)
+        with torch.no_grad():
+            for (name, p), v in zip(mod.named_parameters(), g["params"]):
+                p.copy_(v)
+        x = g["x"].to(DEV).requires_grad_(True)
+        y = mod(x)
+        assert_close(k + ".out", g["out"], y, atol, rtol)
+        ps = [p for _, p in mod.named_parameters()]
+        gr = torch.autograd.grad(y, [x] + ps, g["g_out"].to(DEV), allow_unused=True)
+        for i, (a, b) in enumerate(zip(g["grads"], gr)):
+            if a is None:
+                assert b is None or b.abs().max().item() == 0
+                continue
+            mult = 5 if i == 1 else 1
+            assert_close(f"{k}.grad{i}", a, b, atol * mult, rtol * mult)
+    g = golden["expand_n4"]
+    x = g["x"].to(DEV).requires_grad_(True)
+    y = StreamExpand(g["n"], g["C"])(x)
+    assert torch.equal(y.cpu(), g["out"])
+    (dx,) = torch.autograd.grad(y, x, torch.ones_like(y))
+    assert torch.equal(dx.cpu(), torch.full_like(g["x"], float(g["n"])))
