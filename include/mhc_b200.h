@@ -101,13 +101,19 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C,
  *   out[t, i*C + c] = sum_j h_res[t,i,j] * x[t, j*C + c] + h_post[t,i] * f[t,c]
  * h_res == NULL means H_res = I (no-H_res variant: out = x + h_post (x) f).
  * out has x_dtype.
+ * res_is_logits != 0: h_res holds the raw H_res logits; each token's matrix is
+ * first projected with Sinkhorn-Knopp (sinkhorn_iters, sinkhorn_eps, the same
+ * steps as mhc_sinkhorn_fwd) and, when h_res_out is not NULL, the normalised
+ * matrices are stored there (h_res_dtype) for the backward pass.
  *
- * Replaces: model/mhc_fused.py:736-739 (_post_phase_full_fwd_kernel launch) and
- * model/mhc_fused_no_hres.py:547-550 (_post_phase_fwd_kernel launch).
+ * Replaces: model/mhc_fused.py:736-739 (_post_phase_full_fwd_kernel launch),
+ * with res_is_logits also model/mhc_fused.py:828-830 (sinkhorn_normalize of
+ * h_res_raw), and model/mhc_fused_no_hres.py:547-550 (_post_phase_fwd_kernel).
  */
 int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype,
                  const void *h_post, int h_post_dtype, const void *f, int f_dtype,
-                 void *out, int64_t T, int n, int C, void *stream);
+                 void *out, int64_t T, int n, int C, int res_is_logits, int sinkhorn_iters,
+                 float sinkhorn_eps, void *h_res_out, void *stream);
 
 /*
  * Backward of mhc_post_fwd for upstream gradient dout (x_dtype):
@@ -236,6 +242,32 @@ int mhc_stream_expand_bwd(const void *dout, void *dx, int dtype, int64_t T, int 
 
 /* Number of SMs of the current device (cached per device); <0 on error. */
 int mhc_device_sm_count(void);
+
+/*
+ * Kernel selection for mhc_pre_fwd / mhc_head_fwd.  MHC_PATH_AUTO (default)
+ * uses the fused sm_100a cluster kernel (TMA + tcgen05 + DSMEM) whenever the
+ * call is eligible (bf16 activations, n*C a multiple of 512, C a multiple of
+ * 64, n <= 4 for the full layer, n <= 8 otherwise) and the generic CUDA-core
+ * kernels otherwise; MHC_PATH_GENERIC forces the generic kernels.  Process-wide;
+ * returns the previous policy.  No reference counterpart (reference selected
+ * Triton kernels through environment flags, model/mhc_common.py:25-29).
+ */
+#define MHC_PATH_AUTO    0
+#define MHC_PATH_GENERIC 1
+int mhc_set_path_policy(int policy);
+
+/* 1 if the last mhc_pre_fwd / mhc_head_fwd of the calling thread ran the fused
+ * sm_100a kernel, 0 if it ran the generic kernels. */
+int mhc_last_path(void);
+
+/*
+ * First error code recorded by a fused kernel on the current device (0 = none;
+ * 1..5 = a bounded wait of the producer / MMA / row / coefficient /
+ * pre-aggregate role ran out, which means the kernel gave up instead of
+ * hanging and its outputs are invalid).  Synchronises the device.  clear != 0
+ * resets the word.  No reference counterpart.
+ */
+int mhc_device_error(int clear);
 
 #ifdef __cplusplus
 }

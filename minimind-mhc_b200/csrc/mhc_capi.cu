@@ -51,6 +51,9 @@ static int check_shape(int64_t T, int n, int C) {
   return MHC_OK;
 }
 
+static int g_policy = MHC_PATH_AUTO;
+static thread_local int g_last_path = 0;
+
 static int check_elem_align(const void *p, int dtype, const char *name) {
   if (p && !aligned(p, esize(dtype))) return fail(MHC_ERR_ALIGN, "%s is not %zu-byte aligned", name, esize(dtype));
   return MHC_OK;
@@ -73,6 +76,19 @@ int mhc_abi_version(void) { return 1; }
 const char *mhc_last_error(void) { return g_err; }
 
 int mhc_device_sm_count(void) { return device_sm_count(); }
+
+int mhc_set_path_policy(int policy) {
+  const int prev = g_policy;
+  if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC) g_policy = policy;
+  return prev;
+}
+
+int mhc_last_path(void) { return g_last_path; }
+
+int mhc_device_error(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  return read_tc_error(clear != 0);
+}
 
 size_t mhc_pre_fwd_workspace(int64_t T, int n, int C, int with_res) {
   (void)C;
@@ -111,6 +127,17 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   float *gate = reinterpret_cast<float *>(workspace);
   const int mode = with_res ? 0 : 1;
+  g_last_path = 0;
+  if (g_policy == MHC_PATH_AUTO && pre_tc_eligible(mode, n, x_dtype, x, z, T, C)) {
+    cudaError_t e = launch_pre_tc(mode, n, x, T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr,
+                                  coef_dtype, inv_rms, mixes, s);
+    if (e == cudaSuccess) {
+      g_last_path = 1;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_pre_fwd fused");
+    cudaGetLastError();  // not supported on this device: generic kernels below
+  }
   MHC_TRY(cuda_status(launch_coef_fwd(mode, n, x_dtype, x, T, C, phi, p, h_pre, h_post,
                                       with_res ? h_res : nullptr, coef_dtype, inv_rms, mixes, gate,
                                       device_sm_count(), s),
@@ -120,6 +147,7 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
 
 int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype, const void *h_post,
                  int h_post_dtype, const void *f, int f_dtype, void *out, int64_t T, int n, int C,
+                 int res_is_logits, int sinkhorn_iters, float sinkhorn_eps, void *h_res_out,
                  void *stream) {
   g_err[0] = 0;
   MHC_TRY(check_shape(T, n, C));
@@ -128,11 +156,16 @@ int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype,
     return fail(MHC_ERR_DTYPE, "mhc_post_fwd: bad dtype code");
   if (T == 0) return MHC_OK;
   if (!x || !h_post || !f || !out) return fail(MHC_ERR_NULL, "mhc_post_fwd: required pointer is NULL");
+  if (res_is_logits && (sinkhorn_iters < 0 || sinkhorn_iters > 100000))
+    return fail(MHC_ERR_SHAPE, "mhc_post_fwd: bad sinkhorn_iters %d", sinkhorn_iters);
+  if (h_res_out && !(h_res && res_is_logits))
+    return fail(MHC_ERR_NULL, "mhc_post_fwd: h_res_out needs h_res logits");
   MHC_TRY(check_elem_align(x, x_dtype, "x"));
   MHC_TRY(check_elem_align(out, x_dtype, "out"));
   MHC_TRY(check_elem_align(f, f_dtype, "f"));
   return cuda_status(launch_post_fwd(n, x_dtype, x, h_res, h_res_dtype, h_post, h_post_dtype, f,
-                                     f_dtype, out, T, C, reinterpret_cast<cudaStream_t>(stream)),
+                                     f_dtype, out, T, C, res_is_logits, sinkhorn_iters, sinkhorn_eps,
+                                     h_res_out, reinterpret_cast<cudaStream_t>(stream)),
                      "mhc_post_fwd");
 }
 
@@ -274,6 +307,17 @@ int mhc_head_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void
     return fail(MHC_ERR_WORKSPACE, "mhc_head_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
   CoefParams p{alpha, bias, nullptr, nullptr, nullptr, nullptr, param_dtype, 1.f, pre_eps, rms_eps, 0.f, 0, 0};
   float *gate = reinterpret_cast<float *>(workspace);
+  g_last_path = 0;
+  if (g_policy == MHC_PATH_AUTO && pre_tc_eligible(2, n, x_dtype, x, out, T, C)) {
+    cudaError_t e = launch_pre_tc(2, n, x, T, C, phi, p, out, nullptr, nullptr, nullptr, MHC_F32, inv_rms,
+                                  mix_raw, s);
+    if (e == cudaSuccess) {
+      g_last_path = 1;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_head_fwd fused");
+    cudaGetLastError();
+  }
   MHC_TRY(cuda_status(launch_coef_fwd(2, n, x_dtype, x, T, C, phi, p, nullptr, nullptr, nullptr,
                                       MHC_F32, inv_rms, mix_raw, gate, device_sm_count(), s),
                       "mhc_head_fwd coef"));

@@ -32,9 +32,20 @@ cudaError_t launch_head1_fwd(int x_dtype, const void *x, void *out, float *inv_r
 cudaError_t launch_head1_bwd(int x_dtype, const void *x, const float *inv_rms, const void *dout,
                              void *dx, int64_t T, int C, cudaStream_t stream);
 
+// res_is_logits: h_res holds H_res logits; the kernel applies Sinkhorn-Knopp
+// (sk_iters, sk_eps) per token before the merge and, if h_res_out is given,
+// stores the normalised matrices there (h_res_dtype).
 cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res, int h_res_dtype,
                             const void *h_post, int h_post_dtype, const void *f, int f_dtype,
-                            void *out, int64_t T, int C, cudaStream_t stream);
+                            void *out, int64_t T, int C, int res_is_logits, int sk_iters,
+                            float sk_eps, void *h_res_out, cudaStream_t stream);
+
+// ---- fused sm_100a coefficient + pre-aggregate (bf16 activations) -----------
+bool pre_tc_eligible(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C);
+cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, const void *phi,
+                          const CoefParams &p, void *z, void *h_pre, void *h_post, void *h_res,
+                          int coef_dtype, float *inv_rms, float *mixes, cudaStream_t stream);
+int read_tc_error(bool clear);
 
 cudaError_t launch_post_bwd(int n, int x_dtype, const void *dout, const void *x, const void *h_res,
                             int h_res_dtype, const void *h_post, int h_post_dtype, const void *f,

@@ -13,9 +13,14 @@
 
 namespace mhc {
 
-template <int N, bool HAS_RES>
+// Stage the block's per-token coefficients in shared memory (fp32).  With
+// SK, h_res holds H_res logits: one thread per token runs Sinkhorn-Knopp in
+// registers, writes the normalised matrix back to shared memory and, when
+// h_res_out is given, to global memory for the backward pass.
+template <int N, bool HAS_RES, bool SK>
 __device__ __forceinline__ int stage_post_coefs(float *cs, const void *h_res, int hr_dt, const void *h_post,
-                                                int hp_dt, int64_t T, int64_t tok0, int TB) {
+                                                int hp_dt, int64_t T, int64_t tok0, int TB, int sk_iters,
+                                                float sk_eps, void *h_res_out) {
   constexpr int NCOEF = (HAS_RES ? N * N : 0) + N;
   const int tb = (int)((T - tok0) < TB ? (T - tok0) : TB);
   for (int i = threadIdx.x; i < tb * NCOEF; i += blockDim.x) {
@@ -26,21 +31,37 @@ __device__ __forceinline__ int stage_post_coefs(float *cs, const void *h_res, in
     else v = load_dyn(h_post, hp_dt, tok * N + (k - (HAS_RES ? N * N : 0)));
     cs[i] = v;
   }
+  if constexpr (HAS_RES && SK) {
+    __syncthreads();
+    for (int t = threadIdx.x; t < tb; t += blockDim.x) {
+      float p[N * N];
+      MHC_UNROLL_N
+      for (int k = 0; k < N * N; ++k) p[k] = cs[t * NCOEF + k];
+      sinkhorn_fwd<N>(p, sk_iters, sk_eps);
+      MHC_UNROLL_N
+      for (int k = 0; k < N * N; ++k) {
+        cs[t * NCOEF + k] = p[k];
+        if (h_res_out) store_dyn(h_res_out, hr_dt, (tok0 + t) * (N * N) + k, p[k]);
+      }
+    }
+  }
   __syncthreads();
   return tb;
 }
 
 // 16-byte vector path (x / out in Tx, f in Tf).
-template <int N, typename Tx, typename Tf, bool HAS_RES>
+template <int N, typename Tx, typename Tf, bool HAS_RES, bool SK>
 __global__ void __launch_bounds__(256)
 post_fwd_kernel(const Tx *__restrict__ x, const void *__restrict__ h_res, int hr_dt,
                 const void *__restrict__ h_post, int hp_dt, const Tf *__restrict__ f,
-                Tx *__restrict__ out, int64_t T, int C, int TB) {
+                Tx *__restrict__ out, int64_t T, int C, int TB, int sk_iters, float sk_eps,
+                void *__restrict__ h_res_out) {
   constexpr int VEC = 16 / sizeof(Tx);
   constexpr int NCOEF = (HAS_RES ? N * N : 0) + N;
   extern __shared__ float cs[];  // [TB][NCOEF]
   const int64_t tok0 = (int64_t)blockIdx.x * TB;
-  const int tb = stage_post_coefs<N, HAS_RES>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB);
+  const int tb = stage_post_coefs<N, HAS_RES, SK>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB, sk_iters,
+                                                  sk_eps, h_res_out);
   const int vpt = C / VEC;
   const int64_t nC = (int64_t)N * C;
   const int items = tb * vpt;
@@ -77,15 +98,17 @@ post_fwd_kernel(const Tx *__restrict__ x, const void *__restrict__ h_res, int hr
 }
 
 // Element-wise path for any dtype combination / alignment.
-template <int N, bool HAS_RES>
+template <int N, bool HAS_RES, bool SK>
 __global__ void __launch_bounds__(256)
 post_fwd_scalar_kernel(const void *__restrict__ x, int x_dt, const void *__restrict__ h_res, int hr_dt,
                        const void *__restrict__ h_post, int hp_dt, const void *__restrict__ f, int f_dt,
-                       void *__restrict__ out, int64_t T, int C, int TB) {
+                       void *__restrict__ out, int64_t T, int C, int TB, int sk_iters, float sk_eps,
+                       void *__restrict__ h_res_out) {
   constexpr int NCOEF = (HAS_RES ? N * N : 0) + N;
   extern __shared__ float cs[];
   const int64_t tok0 = (int64_t)blockIdx.x * TB;
-  const int tb = stage_post_coefs<N, HAS_RES>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB);
+  const int tb = stage_post_coefs<N, HAS_RES, SK>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB, sk_iters,
+                                                  sk_eps, h_res_out);
   const int64_t nC = (int64_t)N * C;
   const int items = tb * C;
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
@@ -281,7 +304,8 @@ bool a16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res, int h_res_dtype,
                             const void *h_post, int h_post_dtype, const void *f, int f_dtype,
-                            void *out, int64_t T, int C, cudaStream_t stream) {
+                            void *out, int64_t T, int C, int res_is_logits, int sk_iters,
+                            float sk_eps, void *h_res_out, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const int xvec = x_dtype == MHC_F32 ? 4 : 8;
   const bool vecok = is_vec_pair(x_dtype, f_dtype) && C % xvec == 0 && a16(x) && a16(f) && a16(out);
@@ -290,6 +314,7 @@ cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res
   if (TB > 64) TB = 64;
   if (TB < 1) TB = 1;
   const unsigned grid = (unsigned)((T + TB - 1) / TB);
+  const bool sk = h_res != nullptr && res_is_logits != 0;
   return with_n(n, [&](auto nn) {
     constexpr int N = decltype(nn)::value;
     const size_t smem = (size_t)TB * ((h_res ? N * N : 0) + N) * 4;
@@ -302,20 +327,26 @@ cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res
       return cudaGetLastError();
     };
     if (!vecok) {
+      if (sk)
+        return go(post_fwd_scalar_kernel<N, true, true>, x, x_dtype, h_res, h_res_dtype, h_post, h_post_dtype,
+                  f, f_dtype, out, T, C, TB, sk_iters, sk_eps, h_res_out);
       if (h_res)
-        return go(post_fwd_scalar_kernel<N, true>, x, x_dtype, h_res, h_res_dtype, h_post, h_post_dtype,
-                  f, f_dtype, out, T, C, TB);
-      return go(post_fwd_scalar_kernel<N, false>, x, x_dtype, h_res, h_res_dtype, h_post, h_post_dtype,
-                f, f_dtype, out, T, C, TB);
+        return go(post_fwd_scalar_kernel<N, true, false>, x, x_dtype, h_res, h_res_dtype, h_post, h_post_dtype,
+                  f, f_dtype, out, T, C, TB, sk_iters, sk_eps, h_res_out);
+      return go(post_fwd_scalar_kernel<N, false, false>, x, x_dtype, h_res, h_res_dtype, h_post, h_post_dtype,
+                f, f_dtype, out, T, C, TB, sk_iters, sk_eps, h_res_out);
     }
     return with_vec_pair(x_dtype, f_dtype, [&](auto tx, auto tf) {
       using Tx = decltype(tx);
       using Tf = decltype(tf);
+      if (sk)
+        return go(post_fwd_kernel<N, Tx, Tf, true, true>, (const Tx *)x, h_res, h_res_dtype, h_post,
+                  h_post_dtype, (const Tf *)f, (Tx *)out, T, C, TB, sk_iters, sk_eps, h_res_out);
       if (h_res)
-        return go(post_fwd_kernel<N, Tx, Tf, true>, (const Tx *)x, h_res, h_res_dtype, h_post,
-                  h_post_dtype, (const Tf *)f, (Tx *)out, T, C, TB);
-      return go(post_fwd_kernel<N, Tx, Tf, false>, (const Tx *)x, h_res, h_res_dtype, h_post,
-                h_post_dtype, (const Tf *)f, (Tx *)out, T, C, TB);
+        return go(post_fwd_kernel<N, Tx, Tf, true, false>, (const Tx *)x, h_res, h_res_dtype, h_post,
+                  h_post_dtype, (const Tf *)f, (Tx *)out, T, C, TB, sk_iters, sk_eps, h_res_out);
+      return go(post_fwd_kernel<N, Tx, Tf, false, false>, (const Tx *)x, h_res, h_res_dtype, h_post,
+                h_post_dtype, (const Tf *)f, (Tx *)out, T, C, TB, sk_iters, sk_eps, h_res_out);
     });
   });
 }

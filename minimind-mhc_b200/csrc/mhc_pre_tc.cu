@@ -1,0 +1,652 @@
+// Fused coefficient + pre-aggregate kernel for bf16 activations on sm_100a.
+//
+// One persistent kernel per call, launched as clusters of S = 8 CTAs (one CTA
+// per SM).  A cluster owns a sequence of 128-token tiles; CTA r of the cluster
+// owns K-slice r of the n*C reduction:
+//
+//   warp 0      TMA producer: 128 x 64 bf16 chunks of its x K-slice into an
+//               8-slot ring (128-byte swizzle, 16 KB per slot).
+//   warp 1      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
+//               (M = 128, K = 16 per instruction) into a double-buffered TMEM
+//               accumulator.  phi is split once per launch into bf16 hi | lo
+//               halves (NB = 2*FD padded to 16) held in shared memory for the
+//               whole launch, so the projection is accurate to ~2^-17.
+//   warps 2-5   row warps (thread = token row = TMEM lane): sum of squares of
+//               the slice while the chunks land, then the slice's partial
+//               projection from TMEM; the (FD partials, sum of squares) row is
+//               pushed over DSMEM into the inbox of the CTA that owns that
+//               token's coefficients (16 tokens per CTA).
+//   warp 6      coefficient warp: sums the 8 slices in a fixed order
+//               (deterministic), applies 1/rms, the sigmoid gates and the
+//               H_res affine map, writes the per-token outputs and pushes the
+//               fp32 aggregation weights to all 8 CTAs.
+//   warps 7-14  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] for this
+//               CTA's C/8 columns, re-reading x from L2 (the cluster fetched it
+//               from HBM microseconds earlier).
+//
+// All producer / consumer hand-offs are mbarriers (remote ones arrive with
+// release.cluster); there is no named barrier or other unbounded wait inside
+// the tile loop.  Every wait is bounded (mhc_sm100.cuh) and a timeout sets the
+// device error word, drains the CTA's own async work, frees TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "mhc_device.cuh"
+#include "mhc_dispatch.cuh"
+#include "mhc_kernels.h"
+#include "mhc_sm100.cuh"
+
+namespace mhc {
+
+__device__ int g_tc_error = 0;  // first error code recorded by a fast-path kernel
+
+namespace tc {
+
+using namespace sm100;
+
+constexpr int S = 8;                 // CTAs per cluster (K split)
+constexpr int TM = 128;              // tokens per tile (UMMA M)
+constexpr int RING = 8;              // x chunk slots
+constexpr int CHUNK = TM * 128;      // 128 rows x 128 bytes
+constexpr int TPC = TM / S;          // tokens whose coefficients a CTA finalises
+constexpr int NWARPS = 15, NTHREADS = NWARPS * 32;
+constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_Z = 7, NZW = 8;
+constexpr int TMEM_COLS = 128;            // two accumulators of up to 64 columns
+constexpr int ZU = 3;                     // z items in flight per thread
+
+enum ErrCode { ERR_PROD = 1, ERR_MMA = 2, ERR_ROW = 3, ERR_COEF = 4, ERR_Z = 5 };
+
+template <int N, int MODE>
+struct Cfg {
+  static constexpr int FD = Dims<N, MODE>::FD;
+  static constexpr int NB = ((2 * FD + 15) / 16) * 16;   // hi | lo projection columns
+  static constexpr int IBS = ((FD + 1 + 3) / 4) * 4;     // inbox row: FD partials + sumsq
+  static constexpr int NPAR = 3 + 2 * N + N * N;
+  static constexpr int HPN = N < 4 ? 4 : N;              // weights row (16-byte multiple)
+};
+
+struct Layout {
+  uint32_t ring, phi, inbox, hp, lg, par, bar, tmem, abort, total;
+};
+
+// barrier slots
+constexpr int B_FULL = 0, B_EMPTY = RING, B_ACCF = 2 * RING, B_ACCE = 2 * RING + 2, B_INF = 2 * RING + 4,
+              B_INE = 2 * RING + 6, B_HPF = 2 * RING + 8, B_HPE = 2 * RING + 10, B_ZD = 2 * RING + 12,
+              B_DRAIN = 2 * RING + 14, NBARS = 2 * RING + 15;
+
+__host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR) {
+  Layout L;
+  uint32_t o = 0;
+  L.ring = o;  o += RING * CHUNK;
+  L.phi = o;   o += (uint32_t)CH * NB * 128;
+  L.inbox = o; o += 2u * S * TPC * IBS * 4;
+  L.hp = o;    o += 2u * TM * HPN * 4;
+  L.lg = o;    o += 2u * TPC * 16 * 4;   // H_res logits of the CTA's own tokens (n <= 4)
+  L.par = o;   o += ((NPAR * 4 + 15) / 16) * 16;
+  L.bar = o;   o += NBARS * 8;
+  L.tmem = o;  o += 4;
+  L.abort = o; o += 4;
+  L.total = o;
+  return L;
+}
+
+struct Args {
+  int64_t T;
+  int C, nC, KS, CH;
+  const void *phi;
+  CoefParams p;
+  __nv_bfloat16 *z;
+  void *h_pre, *h_post, *h_res;
+  int coef_dtype;
+  float *inv_rms, *mixes;
+};
+
+// byte offset of element (row j, k) of the phi slice: chunk-major, 128-byte
+// swizzled K-major rows (granule index XOR row-in-atom)
+__device__ __forceinline__ uint32_t phi_off(int j, int k, int NB) {
+  const int c = k >> 6, kk = k & 63;
+  return (uint32_t)c * NB * 128 + (j >> 3) * 1024 + (j & 7) * 128 + ((((kk >> 3) ^ (j & 7))) << 4) + ((kk & 7) << 1);
+}
+
+__device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
+  *abort_flag = 1;
+  atomicCAS(&g_tc_error, 0, code);
+}
+
+__device__ __forceinline__ float sq8(uint4 v) {
+  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    s = fmaf(f.x, f.x, s);
+    s = fmaf(f.y, f.y, s);
+  }
+  return s;
+}
+
+template <int N, int MODE>
+__device__ __forceinline__ void load_params_tc(float *par, const CoefParams &p, int tid, int nthreads) {
+  constexpr int NPAR = 3 + 2 * N + N * N;
+  for (int i = tid; i < NPAR; i += nthreads) {
+    float v = 0.f;
+    const int dt = p.param_dtype;
+    if (i == 0) v = load_dyn(p.alpha_pre, dt, 0);
+    else if (i == 1) { if (MODE != HEAD) v = load_dyn(p.alpha_post, dt, 0); }
+    else if (i == 2) { if (MODE == FULL) v = load_dyn(p.alpha_res, dt, 0); }
+    else if (i < 3 + N) v = load_dyn(p.bias_pre, dt, i - 3);
+    else if (i < 3 + 2 * N) { if (MODE != HEAD) v = load_dyn(p.bias_post, dt, i - 3 - N); }
+    else { if (MODE == FULL) v = load_dyn(p.bias_res, dt, i - 3 - 2 * N); }
+    par[i] = v;
+  }
+}
+
+template <int N, int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1)
+pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__restrict__ x, Args a) {
+  using Cf = Cfg<N, MODE>;
+  constexpr int FD = Cf::FD, NB = Cf::NB, IBS = Cf::IBS, NPAR = Cf::NPAR, HPN = Cf::HPN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t *base = smem_raw + (base_u32 - raw_u32);
+  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR);
+  float *inbox = reinterpret_cast<float *>(base + L.inbox);
+  float *hp = reinterpret_cast<float *>(base + L.hp);
+  float *par = reinterpret_cast<float *>(base + L.par);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(base + L.abort);
+  const uint32_t bar0 = base_u32 + L.bar;
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+// warp-uniform bounded wait: every lane waits (and so acquires), the warp
+// agrees on the outcome so it always leaves a loop together
+#define WAIT_WARP(CL, bar, par) (__all_sync(0xffffffffu, wait_parity<CL>((bar), (par), abort_flag)))
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank(), cid = cluster_id_x(), ncl = ncluster_x();
+  const int ntiles = (int)((a.T + TM - 1) / TM);
+  const int CH = a.CH;
+
+  // ---------------- prologue ----------------
+  if (tid == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(BAR(B_FULL + i), 1);
+      mbar_init(BAR(B_EMPTY + i), 1 + 4);  // MMA commit + 4 row warps
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(B_ACCF + b), 1);
+      mbar_init(BAR(B_ACCE + b), 4);
+      mbar_init(BAR(B_INF + b), S);  // one per source CTA (its half-warp of owned rows)
+      mbar_init(BAR(B_INE + b), S);  // one per owner CTA (inbox rows consumed)
+      mbar_init(BAR(B_HPF + b), S);  // one per source CTA (its 16 tokens' weights)
+      mbar_init(BAR(B_HPE + b), S);  // one per CTA's pre-aggregate group
+      mbar_init(BAR(B_ZD + b), NZW);       // local: pre-aggregate warps done
+    }
+    mbar_init(BAR(B_DRAIN), 1);
+    fence_mbar_init_cluster();
+  }
+  if (warp == W_MMA) {
+    tmem_alloc(base_u32 + L.tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  {
+    // phi slice of this CTA -> bf16 hi | lo, K-major, 128-byte swizzle
+    const int k0 = (int)rank * a.KS;
+    uint8_t *phs = base + L.phi;
+    for (int e = tid; e < a.KS * FD; e += NTHREADS) {
+      const int k = e / FD, j = e - k * FD;
+      const float v = load_dyn(a.phi, a.p.param_dtype, (int64_t)(k0 + k) * FD + j);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+      *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = hi;
+      *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j + FD, k, NB)) = lo;
+    }
+    constexpr int PADR = NB - 2 * FD;
+    if constexpr (PADR > 0) {
+      for (int e = tid; e < a.KS * PADR; e += NTHREADS) {
+        const int k = e / PADR, j = 2 * FD + (e - (e / PADR) * PADR);
+        *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = __float2bfloat16_rn(0.f);
+      }
+    }
+    load_params_tc<N, MODE>(par, a.p, tid, NTHREADS);
+  }
+  fence_proxy_async_smem();  // generic phi writes -> tensor-core (async proxy) reads
+  __syncthreads();
+  cluster_sync_all();        // every CTA's barriers exist before any remote arrive
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
+
+  if (warp == W_PROD) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t q = 0;
+      bool ok = true;
+      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl) {
+        for (int c = 0; c < CH; ++c, ++q) {
+          const uint32_t slot = q % RING, ph = (q / RING) & 1u;
+          if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
+          tma_load_2d(base_u32 + L.ring + slot * CHUNK, &tmap, (int)rank * a.KS + c * 64, tile * TM,
+                      BAR(B_FULL + slot));
+        }
+      }
+      if (!ok) record_error(ERR_PROD, abort_flag);
+      // copies in flight must land before the CTA can exit
+      const uint32_t q0 = q > (uint32_t)RING ? q - RING : 0u;
+      for (uint32_t p = q0; p < q; ++p) wait_parity<false>(BAR(B_FULL + p % RING), (p / RING) & 1u, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == W_MMA) {
+    // ---------------- tcgen05 MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(128, NB);
+      uint32_t q = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+        const int buf = lt & 1;
+        const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
+        if (!wait_parity<false>(BAR(B_ACCE + buf), aph ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + (uint32_t)buf * 64u;
+        for (int c = 0; c < CH; ++c, ++q) {
+          const uint32_t slot = q % RING, ph = (q / RING) & 1u;
+          if (!wait_parity<false>(BAR(B_FULL + slot), ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = base_u32 + L.ring + slot * CHUNK;
+          const uint32_t b0 = base_u32 + L.phi + (uint32_t)c * NB * 128u;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(dcol, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
+                      (c | k) != 0 ? 1u : 0u);
+          umma_commit(BAR(B_EMPTY + slot));
+        }
+        if (!ok) break;
+        umma_commit(BAR(B_ACCF + buf));
+      }
+      if (!ok) record_error(ERR_MMA, abort_flag);
+      // every issued MMA completes before TMEM is released
+      umma_commit(BAR(B_DRAIN));
+      wait_parity<false>(BAR(B_DRAIN), 0u, nullptr);
+    }
+    __syncwarp();
+  } else if (warp >= W_ROW && warp < W_ROW + 4) {
+    // ---------------- row warps ----------------
+    const int quad = warp & 3;            // TMEM lane quadrant of this warp
+    const int row = quad * 32 + lane;     // token row of the tile = TMEM lane
+    uint32_t q = 0;
+    int lt = 0;
+    bool ok = true;
+    for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+      float ss = 0.f;
+      for (int c = 0; c < CH; ++c, ++q) {
+        const uint32_t slot = q % RING, ph = (q / RING) & 1u;
+        if (!WAIT_WARP(false, BAR(B_FULL + slot), ph)) { ok = false; break; }
+        const uint8_t *rp = base + L.ring + slot * CHUNK + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ss += sq8(*reinterpret_cast<const uint4 *>(rp + ((u ^ (row & 7)) << 4)));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(B_EMPTY + slot));
+      }
+      if (!ok) break;
+      const int buf = lt & 1;
+      const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
+      if (!WAIT_WARP(false, BAR(B_ACCF + buf), aph)) { ok = false; break; }
+      tc_fence_after();
+      float d[NB];
+#pragma unroll
+      for (int c16 = 0; c16 < NB / 16; ++c16) {
+        float t16[16];
+        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * 64u + (uint32_t)c16 * 16u, t16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[c16 * 16 + i] = t16[i];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(B_ACCE + buf));
+      float vals[IBS];
+#pragma unroll
+      for (int j = 0; j < IBS; ++j) vals[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < FD; ++j) vals[j] = d[j] + d[FD + j];
+      vals[FD] = ss;
+      // the owner's inbox slot for this buffer must have been drained
+      if (!WAIT_WARP(true, BAR(B_INE + buf), aph ^ 1u)) { ok = false; break; }
+      const uint32_t owner = (uint32_t)(row / TPC);
+      const uint32_t dst = mapa(base_u32 + L.inbox + (uint32_t)(((buf * S + (int)rank) * TPC + (row % TPC)) * IBS * 4),
+                                owner);
+#pragma unroll
+      for (int v = 0; v < IBS / 4; ++v)
+        st_cluster_v4(dst + v * 16, vals[4 * v], vals[4 * v + 1], vals[4 * v + 2], vals[4 * v + 3]);
+      // publish: every lane fences its own stores at cluster scope, then one
+      // lane per half-warp (16 rows = one owner) arrives with release
+      fence_acq_rel_cluster();
+      __syncwarp();
+      if ((lane & 15) == 0) mbar_arrive_cluster(mapa(BAR(B_INF + buf), owner));
+    }
+    if (!ok) record_error(ERR_ROW, abort_flag);
+  } else if (warp == W_COEF) {
+    // ---------------- coefficient warp ----------------
+    float *lg = reinterpret_cast<float *>(base + L.lg);
+    int lt = 0;
+    bool ok = true;
+    for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+      const int buf = lt & 1;
+      const uint32_t ph = (uint32_t)(lt >> 1) & 1u;
+      if (!WAIT_WARP(true, BAR(B_INF + buf), ph)) { ok = false; break; }
+      float acc[FD + 1];
+#pragma unroll
+      for (int j = 0; j <= FD; ++j) acc[j] = 0.f;
+      if (lane < TPC) {
+#pragma unroll 1
+        for (int s = 0; s < S; ++s) {  // fixed order over the K slices: deterministic
+          const float *src = inbox + ((buf * S + s) * TPC + lane) * IBS;
+#pragma unroll
+          for (int j = 0; j <= FD; ++j) acc[j] += src[j];
+        }
+      }
+      __syncwarp();
+      if (lane < S) mbar_arrive_remote(mapa(BAR(B_INE + buf), (uint32_t)lane));  // inbox rows free again
+      const int t = (int)rank * TPC + lane;  // token row of the tile
+      const int64_t tok = (int64_t)tile * TM + t;
+      const bool live = lane < TPC && tok < a.T;
+      float w[HPN], m[FD], ho[N];
+      float inv = 0.f;
+#pragma unroll
+      for (int i = 0; i < HPN; ++i) w[i] = 0.f;
+      // this CTA's weights and logits buffers of `buf` must be free (pre-aggregate of tile lt-2 done)
+      if (!WAIT_WARP(true, BAR(B_HPE + buf), ph ^ 1u)) { ok = false; break; }
+      if (lane < TPC) {
+        inv = 1.0f / sqrtf(acc[FD] / (float)a.nC + a.p.rms_eps);
+#pragma unroll
+        for (int j = 0; j < FD; ++j) m[j] = acc[j] * inv;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          w[i] = sigmoidf_(__fadd_rn(__fmul_rn(m[i], par[0]), par[3 + i])) + a.p.pre_eps;
+          if constexpr (MODE != HEAD)
+            ho[i] = sigmoidf_(__fadd_rn(__fmul_rn(m[N + i], par[1]), par[3 + N + i])) * a.p.post_mult;
+        }
+        if constexpr (MODE == FULL) {
+          float *lrow = lg + (buf * TPC + lane) * 16;
+#pragma unroll
+          for (int k = 0; k < N * N; ++k) lrow[k] = __fadd_rn(__fmul_rn(m[2 * N + k], par[2]), par[3 + 2 * N + k]);
+        }
+        // publish the aggregation weights to every CTA of the cluster
+        const uint32_t loc = base_u32 + L.hp + (uint32_t)((buf * TM + t) * HPN * 4);
+#pragma unroll 1
+        for (int dcta = 0; dcta < S; ++dcta) {
+          const uint32_t dst = mapa(loc, (uint32_t)dcta);
+#pragma unroll
+          for (int v = 0; v < HPN / 4; ++v) st_cluster_v4(dst + v * 16, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+        }
+      }
+      fence_acq_rel_cluster();
+      __syncwarp();
+      if (lane < S) mbar_arrive_cluster(mapa(BAR(B_HPF + buf), (uint32_t)lane));
+      // per-token outputs (after the hand-off so they do not delay it)
+      if (live) {
+        a.inv_rms[tok] = inv;
+#pragma unroll
+        for (int j = 0; j < FD; ++j) a.mixes[tok * FD + j] = m[j];
+        if constexpr (MODE != HEAD) {
+#pragma unroll
+          for (int i = 0; i < N; ++i) {
+            if (a.h_pre) store_dyn(a.h_pre, a.coef_dtype, tok * N + i, w[i]);
+            store_dyn(a.h_post, a.coef_dtype, tok * N + i, ho[i]);
+          }
+        }
+      }
+    }
+    if (!ok) record_error(ERR_COEF, abort_flag);
+  } else {
+    // ---------------- pre-aggregate warps (+ Sinkhorn of the CTA's own tokens) ----------------
+    const float *lg = reinterpret_cast<const float *>(base + L.lg);
+    const int ztid = tid - W_Z * 32;
+    const int cz = a.C / S;      // columns of z owned by this CTA
+    const int vpr = cz / 8;      // 16-byte vectors per row
+    const int c0 = (int)rank * cz;
+    const int items = TM * vpr;
+    constexpr int NN = N * N;    // threads per token in the Sinkhorn step
+    int lt = 0;
+    bool ok = true;
+    for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+      const int buf = lt & 1;
+      const uint32_t ph = (uint32_t)(lt >> 1) & 1u;
+      if (!WAIT_WARP(true, BAR(B_HPF + buf), ph)) { ok = false; break; }
+      const float *hps = hp + buf * TM * HPN;
+      uint4 raw[ZU][N];
+      auto load_round = [&](int it0) {
+#pragma unroll
+        for (int u = 0; u < ZU; ++u) {
+          const int it = it0 + u * NZW * 32;
+          const int t = it / vpr;
+          const int64_t tk = (int64_t)tile * TM + t;
+          if (it < items && tk < a.T) {
+            const __nv_bfloat16 *xr = x + tk * a.nC + c0 + (it - t * vpr) * 8;
+#pragma unroll
+            for (int i = 0; i < N; ++i) raw[u][i] = __ldcs(reinterpret_cast<const uint4 *>(xr + (int64_t)i * a.C));
+          }
+        }
+      };
+      auto consume_round = [&](int it0) {
+#pragma unroll
+        for (int u = 0; u < ZU; ++u) {
+          const int it = it0 + u * NZW * 32;
+          const int t = it / vpr;
+          const int v = it - t * vpr;
+          const int64_t tk = (int64_t)tile * TM + t;
+          if (it < items && tk < a.T) {
+            float acc[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+              const float wi = hps[t * HPN + i];
+              Pack<__nv_bfloat16> pk;
+              pk.raw = raw[u][i];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[e] = fmaf(wi, pk.get(e), acc[e]);
+            }
+            Pack<__nv_bfloat16> o;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o.set(e, acc[e]);
+            *reinterpret_cast<uint4 *>(a.z + tk * a.C + c0 + v * 8) = o.raw;
+          }
+        }
+      };
+      load_round(ztid);
+      if constexpr (MODE == FULL) {
+        // while the first loads are in flight: H_res of the CTA's 16 tokens, one
+        // matrix element per thread, row / column sums over lane shuffles (all
+        // 256 threads take part so every shuffle has a full warp)
+        const int sk_t = ztid / NN, e = ztid % NN;
+        const bool sk_live = sk_t < TPC;
+        float v = sk_live ? lg[(buf * TPC + sk_t) * 16 + e] : 0.f;
+        if (a.p.apply_sinkhorn) {
+          float mx = v;
+#pragma unroll
+          for (int o = 1; o < N; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          const float ex = expf(v - mx);
+          float rs = ex;
+#pragma unroll
+          for (int o = 1; o < N; o <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+          v = ex * (1.0f / rs) + a.p.sk_eps;
+          float cs = v;
+#pragma unroll
+          for (int o = N; o < NN; o <<= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+          v = v * (1.0f / (cs + a.p.sk_eps));
+          for (int itr = 1; itr < a.p.sk_iters; ++itr) {
+            float r = v;
+#pragma unroll
+            for (int o = 1; o < N; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+            v = v * (1.0f / (r + a.p.sk_eps));
+            float c = v;
+#pragma unroll
+            for (int o = N; o < NN; o <<= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+            v = v * (1.0f / (c + a.p.sk_eps));
+          }
+        }
+        const int64_t sk_tok = (int64_t)tile * TM + (int)rank * TPC + sk_t;
+        if (sk_live && sk_tok < a.T && a.h_res) store_dyn(a.h_res, a.coef_dtype, sk_tok * NN + e, v);
+      }
+      consume_round(ztid);
+      for (int it0 = ztid + ZU * NZW * 32; it0 < items; it0 += ZU * NZW * 32) {
+        load_round(it0);
+        consume_round(it0);
+      }
+      // this CTA is done reading the weights / logits of `buf`: tell every writer
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(B_ZD + buf));
+      if (warp == W_Z) {
+        int good = 1;
+        if (lane == 0) {
+          good = wait_parity<false>(BAR(B_ZD + buf), ph, abort_flag) ? 1 : 0;
+          if (good)
+            for (int s = 0; s < S; ++s) mbar_arrive_remote(mapa(BAR(B_HPE + buf), (uint32_t)s));
+        }
+        if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+      }
+    }
+    if (!ok) record_error(ERR_Z, abort_flag);
+  }
+
+  // ---------------- teardown ----------------
+  __syncthreads();
+  if (warp == W_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  cluster_sync_all();  // no CTA leaves while a peer may still touch its shared memory
+#undef WAIT_WARP
+#undef BAR
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <int N, int MODE>
+static cudaError_t launch_impl(const void *x, int64_t T, int C, const Args &args, cudaStream_t stream) {
+  using Cf = Cfg<N, MODE>;
+  const int nC = N * C;
+  const Layout L = make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR);
+  const size_t smem = (size_t)L.total + 1024;
+  auto kern = pre_tc_kernel<N, MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+
+  CUtensorMap tmap;
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
+  const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)TM};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorNotSupported;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  static int max_clusters[64][3][5];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int ni = N == 1 ? 0 : N == 2 ? 1 : N == 4 ? 2 : N == 8 ? 3 : 4;
+  int &mc = max_clusters[dev & 63][MODE][ni];
+  if (mc == 0) {
+    cfg.gridDim = dim3(S * 64, 1, 1);
+    int v = 0;
+    e = cudaOccupancyMaxActiveClusters(&v, (void *)kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (v <= 0) return cudaErrorNotSupported;
+    mc = v;
+  }
+  const int64_t ntiles = (T + TM - 1) / TM;
+  const int clusters = (int)(ntiles < mc ? ntiles : mc);
+  cfg.gridDim = dim3((unsigned)(clusters * S), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+bool pre_tc_eligible(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C) {
+  if (x_dtype != MHC_BF16 || T < 1) return false;
+  const int fd = mode == FULL ? 2 * n + n * n : (mode == NOHRES ? 2 * n : n);
+  if (mode == FULL && n > 4) return false;
+  if (mode != FULL && n > 8) return false;
+  if (mode == HEAD && n < 2) return false;
+  if (fd + 1 > 28) return false;
+  const int64_t nC = (int64_t)n * C;
+  if (nC % (tc::S * 64) != 0 || C % (tc::S * 8) != 0) return false;
+  if (nC / tc::S / 64 > 8) return false;  // phi slice budget
+  if (((uintptr_t)x & 15) != 0 || ((uintptr_t)z & 15) != 0) return false;
+  return true;
+}
+
+cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, const void *phi,
+                          const CoefParams &p, void *z, void *h_pre, void *h_post, void *h_res,
+                          int coef_dtype, float *inv_rms, float *mixes, cudaStream_t stream) {
+  tc::Args a;
+  a.T = T;
+  a.C = C;
+  a.nC = n * C;
+  a.KS = n * C / tc::S;
+  a.CH = a.KS / 64;
+  a.phi = phi;
+  a.p = p;
+  a.z = reinterpret_cast<__nv_bfloat16 *>(z);
+  a.h_pre = h_pre;
+  a.h_post = h_post;
+  a.h_res = h_res;
+  a.coef_dtype = coef_dtype;
+  a.inv_rms = inv_rms;
+  a.mixes = mixes;
+  return with_mode(mode, [&](auto md) -> cudaError_t {
+    constexpr int MODE = decltype(md)::value;
+    switch (n) {
+      case 1: if constexpr (MODE == FULL) return tc::launch_impl<1, MODE>(x, T, C, a, stream); break;
+      case 2: if constexpr (MODE != HEAD || true) return tc::launch_impl<2, MODE>(x, T, C, a, stream); break;
+      case 4: return tc::launch_impl<4, MODE>(x, T, C, a, stream);
+      case 8: if constexpr (MODE != FULL) return tc::launch_impl<8, MODE>(x, T, C, a, stream); break;
+      default: break;
+    }
+    return cudaErrorNotSupported;
+  });
+}
+
+int read_tc_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace mhc

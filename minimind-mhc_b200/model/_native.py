@@ -35,7 +35,7 @@ _PROTOS = {
     "mhc_pre_fwd_workspace": (_SZ, [_I64, _I, _I, _I]),
     "mhc_pre_fwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
                          _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),
-    "mhc_post_fwd": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _I64, _I, _I, _P]),
+    "mhc_post_fwd": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _I64, _I, _I, _I, _I, _F, _P, _P]),
     "mhc_post_bwd": (_I, [_P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _I64, _I, _I, _P]),
     "mhc_pre_bwd_workspace": (_SZ, [_I64, _I, _I, _I, _I, _I]),
     "mhc_pre_bwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
@@ -50,7 +50,12 @@ _PROTOS = {
                           _P, _P, _SZ, _P]),
     "mhc_stream_expand_fwd": (_I, [_P, _P, _I, _I64, _I, _I, _P]),
     "mhc_stream_expand_bwd": (_I, [_P, _P, _I, _I64, _I, _I, _P]),
+    "mhc_set_path_policy": (_I, [_I]),
+    "mhc_last_path": (_I, []),
+    "mhc_device_error": (_I, [_I]),
 }
+
+PATH_AUTO, PATH_GENERIC = 0, 1
 
 EXPORTED = tuple(_PROTOS)
 

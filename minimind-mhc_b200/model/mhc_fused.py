@@ -208,7 +208,7 @@ class _PostPhaseFullFn(torch.autograd.Function):
         out = torch.empty_like(xc)
         nat.call("mhc_post_fwd", nat.ptr(xc), nat.dtype_code(xc.dtype), nat.ptr(hr),
                  nat.dtype_code(hr.dtype), nat.ptr(hp), nat.dtype_code(hp.dtype), nat.ptr(fc),
-                 nat.dtype_code(fc.dtype), nat.ptr(out), t, n, c, nat.stream_of(xc))
+                 nat.dtype_code(fc.dtype), nat.ptr(out), t, n, c, 0, 0, 0.0, None, nat.stream_of(xc))
         ctx.save_for_backward(xc, hr, hp, fc)
         ctx.meta = (b, l, n, c)
         return out.view(b, l, nc)
@@ -254,6 +254,8 @@ class _MHCPreFn(torch.autograd.Function):
         x2d = x_flat.contiguous().view(b * l, nc)
         raw = [w_phi, alpha_pre, bias_pre, alpha_post, bias_post] + ([alpha_res, bias_res] if with_res else [])
         ps = _params(*raw)
+        # the coefficient kernel applies Sinkhorn-Knopp itself (fp32 H_res out);
+        # backward differentiates it by recompute
         z, _, h_post, h_res, inv_rms, mixes = _pre_fwd(
             x2d, ps, with_res, with_res, iters, post_mult, pre_eps, rms_eps, sk_eps, n, c,
             torch.float32, False)
@@ -289,17 +291,17 @@ class _MHCPreFn(torch.autograd.Function):
 
 class _MHCPostFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_flat, h_res, h_post, f_out, link, with_res, n, c):
+    def forward(ctx, x_flat, h_res, h_post, f_out, link, with_res, iters, sk_eps, n, c):
         nat.require_cuda(x_flat, h_post, f_out)
         b, l, nc = x_flat.shape
         t = b * l
         xc = x_flat.contiguous().view(t, nc)
         fc = f_out.contiguous().view(t, c)
-        hr = h_res if with_res else None
         out = torch.empty_like(xc)
+        hr = h_res if with_res else None
         nat.call("mhc_post_fwd", nat.ptr(xc), nat.dtype_code(xc.dtype), nat.ptr(hr), nat.F32,
                  nat.ptr(h_post), nat.F32, nat.ptr(fc), nat.dtype_code(fc.dtype), nat.ptr(out),
-                 t, n, c, nat.stream_of(xc))
+                 t, n, c, 0, 0, 0.0, None, nat.stream_of(xc))
         ctx.save_for_backward(xc, h_res if with_res else h_post.new_empty(0), h_post, fc)
         ctx.meta = (b, l, n, c, bool(with_res))
         ctx.link = link
@@ -328,7 +330,7 @@ class _MHCPostFn(torch.autograd.Function):
                      nat.F32, nat.ptr(hp), nat.F32, nat.ptr(fc), nat.dtype_code(fc.dtype), None,
                      None, nat.ptr(dhp), nat.ptr(df), t, n, c, nat.stream_of(xc))
             ctx.link.dx_post = gc  # H_res = I: the residual gradient is g itself
-        return None, dhr, dhp, df.view(b, l, c), None, None, None, None
+        return None, dhr, dhp, df.view(b, l, c), None, None, None, None, None, None
 
 
 def mhc_connection(x_flat, sublayer_fn, phi, alpha_pre, bias_pre, alpha_post, bias_post,
@@ -340,7 +342,8 @@ def mhc_connection(x_flat, sublayer_fn, phi, alpha_pre, bias_pre, alpha_post, bi
                                         alpha_res, bias_res, link, with_res, sinkhorn_iters,
                                         post_mult, pre_eps, eps, sinkhorn_eps, n, c)
     f_out = sublayer_fn(z)
-    return _MHCPostFn.apply(x_flat, h_res, h_post, f_out, link, with_res, n, c)
+    return _MHCPostFn.apply(x_flat, h_res, h_post, f_out, link, with_res, sinkhorn_iters,
+                            sinkhorn_eps, n, c)
 
 
 class MHCConnection_Fused(nn.Module):

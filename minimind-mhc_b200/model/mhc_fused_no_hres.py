@@ -81,7 +81,7 @@ class _PostPhaseFn(torch.autograd.Function):
         out = torch.empty_like(xc)
         nat.call("mhc_post_fwd", nat.ptr(xc), nat.dtype_code(xc.dtype), None, nat.F32, nat.ptr(hp),
                  nat.dtype_code(hp.dtype), nat.ptr(fc), nat.dtype_code(fc.dtype), nat.ptr(out),
-                 t, n, c, nat.stream_of(xc))
+                 t, n, c, 0, 0, 0.0, None, nat.stream_of(xc))
         ctx.save_for_backward(hp, fc)
         ctx.meta = (b, l, n, c, xc.dtype)
         return out.view(b, l, nc)

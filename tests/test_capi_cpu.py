@@ -52,17 +52,20 @@ def test_library_exports_every_declared_symbol(lib):
 def test_host_validation_rejects_bad_arguments(lib):
     P = ctypes.c_void_p(16)  # never dereferenced: validation fails first
     # bad n
-    st = lib.mhc_post_fwd(P, 1, P, 0, P, 0, P, 1, P, 8, 3, 64, None)
+    st = lib.mhc_post_fwd(P, 1, P, 0, P, 0, P, 1, P, 8, 3, 64, 0, 0, 0.0, None, None)
     assert st == -3 and b"n must be" in lib.mhc_last_error()
     # bad dtype
-    st = lib.mhc_post_fwd(P, 7, P, 0, P, 0, P, 1, P, 8, 4, 64, None)
+    st = lib.mhc_post_fwd(P, 7, P, 0, P, 0, P, 1, P, 8, 4, 64, 0, 0, 0.0, None, None)
     assert st == -2
     # NULL input
-    st = lib.mhc_post_fwd(None, 1, None, 0, P, 0, P, 1, P, 8, 4, 64, None)
+    st = lib.mhc_post_fwd(None, 1, None, 0, P, 0, P, 1, P, 8, 4, 64, 0, 0, 0.0, None, None)
     assert st == -1
     # misaligned bf16 pointer
-    st = lib.mhc_post_fwd(ctypes.c_void_p(17), 1, None, 0, P, 0, P, 1, P, 8, 4, 64, None)
+    st = lib.mhc_post_fwd(ctypes.c_void_p(17), 1, None, 0, P, 0, P, 1, P, 8, 4, 64, 0, 0, 0.0, None, None)
     assert st == -4
+    # h_res_out without logits
+    st = lib.mhc_post_fwd(P, 1, None, 0, P, 0, P, 1, P, 8, 4, 64, 0, 0, 0.0, P, None)
+    assert st == -1
     # pre_fwd: workspace too small
     st = lib.mhc_pre_fwd(P, 1, 8, 4, 64, P, P, P, P, P, P, P, 0, 1, 1, 20, 2.0, 1e-6, 1e-6, 1e-6,
                          P, None, P, P, 0, P, P, P, 0, None)
@@ -78,9 +81,16 @@ def test_host_validation_rejects_bad_arguments(lib):
 
 def test_empty_batch_is_a_no_op(lib):
     # T == 0 returns OK without touching any pointer or the device
-    assert lib.mhc_post_fwd(None, 1, None, 0, None, 0, None, 1, None, 0, 4, 64, None) == 0
+    assert lib.mhc_post_fwd(None, 1, None, 0, None, 0, None, 1, None, 0, 4, 64, 0, 0, 0.0, None, None) == 0
     assert lib.mhc_sinkhorn_fwd(None, 0, None, 0, 0, 4, 20, 1e-6, None) == 0
     assert lib.mhc_stream_expand_fwd(None, None, 1, 0, 4, 64, None) == 0
+
+
+def test_path_policy_switch(lib):
+    prev = lib.mhc_set_path_policy(1)
+    assert lib.mhc_set_path_policy(0) == 1
+    lib.mhc_set_path_policy(prev)
+    assert lib.mhc_set_path_policy(prev) == prev
 
 
 def test_workspace_queries(lib):

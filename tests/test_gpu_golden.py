@@ -59,7 +59,7 @@ def test_post_phase_full_golden(golden):
     for k in [k for k in golden if k.startswith("post_full_")]:
         g = golden[k]
         f32 = g["x"].dtype == torch.float32
-        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 5e-3)
+        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 1e-2)
         leaves = [t.to(DEV).requires_grad_(True) for t in (g["x"], g["h_res"], g["h_post"], g["f"])]
         o = _PostPhaseFullFn.apply(*leaves, g["n"], g["C"])
         assert_close(k + ".out", g["out"], o, atol, rtol)
@@ -115,7 +115,9 @@ def test_no_hres_golden(golden):
     for k in [k for k in golden if k.startswith("post_nohres_")]:
         g = golden[k]
         f32 = g["x"].dtype == torch.float32
-        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 5e-3)
+        # bf16: the reference's 5e-2 abs, and the 1e-2 relative bar for bf16 streams
+        # (a 1-ulp bf16 difference at |v| ~ 12 is 6e-2 abs / 5.2e-3 rel)
+        atol, rtol = (1e-5, 1e-5) if f32 else (5e-2, 1e-2)
         leaves = [t.to(DEV).requires_grad_(True) for t in (g["x"], g["h_post"], g["f"])]
         o = _PostPhaseFn.apply(*leaves, g["n"], g["C"])
         assert_close(k + ".out", g["out"], o, atol, rtol)

@@ -91,7 +91,7 @@ def test_config2_shape_coefficients_and_streams(with_res):
     out = torch.empty_like(xd)
     fd = f.to(DEV)
     nat.call("mhc_post_fwd", nat.ptr(xd), nat.BF16, nat.ptr(h_res) if with_res else None, nat.F32,
-             nat.ptr(h_post), nat.F32, nat.ptr(fd), nat.BF16, nat.ptr(out), t, n, c,
+             nat.ptr(h_post), nat.F32, nat.ptr(fd), nat.BF16, nat.ptr(out), t, n, c, 0, 0, 0.0, None,
              torch.cuda.current_stream().cuda_stream)
     if with_res:
         ro = O.post_phase_full(x.float(), ref["h_res"], ref["h_post"], f.float(), n, c)
