@@ -128,7 +128,18 @@ __device__ __forceinline__ void store_vec_stream(T *p, const float (&v)[V]) {
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
+// Hardware reciprocal (rcp.approx.ftz.f32, within 1 ulp for normal inputs).
+// The reference's Triton kernels divide with Triton's default fp32 division,
+// which is approximate as well (model/mhc_fused.py:86-91, 210, 252-253); the
+// IEEE-rounded reciprocal is a multi-instruction sequence that made the
+// 20-iteration Sinkhorn about 3.5x slower.
+__device__ __forceinline__ float fast_rcp(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ float sigmoidf_(float v) { return fast_rcp(1.0f + expf(-v)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -140,8 +151,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Sinkhorn-Knopp on an N x N matrix held in registers (row-major p[i*N+j]).
 // Same step order as the reference: softmax(-1) + eps, column normalisation,
 // then (iters - 1) x [row, column] normalisations, each x / (sum + eps).  Each
-// normalisation takes one IEEE reciprocal of (sum + eps) per row / column and
-// multiplies by it (within 1.5 ulp of a per-element division).
+// normalisation takes one hardware reciprocal of (sum + eps) per row / column
+// and multiplies by it (within 2 ulp of a per-element division).
 // ---------------------------------------------------------------------------
 template <int N>
 __device__ __forceinline__ void sk_row_norm(float (&p)[N * N], float eps) {
@@ -150,7 +161,7 @@ MHC_UNROLL_N
     float s = 0.f;
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) s += p[i * N + j];
-    const float r = __frcp_rn(s + eps);
+    const float r = fast_rcp(s + eps);
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) p[i * N + j] = p[i * N + j] * r;
   }
@@ -163,7 +174,7 @@ MHC_UNROLL_N
     float s = 0.f;
 MHC_UNROLL_N
     for (int i = 0; i < N; ++i) s += p[i * N + j];
-    const float r = __frcp_rn(s + eps);
+    const float r = fast_rcp(s + eps);
 MHC_UNROLL_N
     for (int i = 0; i < N; ++i) p[i * N + j] = p[i * N + j] * r;
   }
@@ -184,7 +195,7 @@ MHC_UNROLL_N
       p[i * N + j] = e;
       s += e;
     }
-    const float r = __frcp_rn(s);
+    const float r = fast_rcp(s);
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) p[i * N + j] = p[i * N + j] * r;
   }
@@ -211,7 +222,7 @@ MHC_UNROLL_N
     float s = 0.f;
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) s += a[i * N + j];
-    const float r = __frcp_rn(s + eps);
+    const float r = fast_rcp(s + eps);
     float dot = 0.f;
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) dot += g[i * N + j] * (a[i * N + j] * r);
@@ -227,7 +238,7 @@ MHC_UNROLL_N
     float s = 0.f;
 MHC_UNROLL_N
     for (int i = 0; i < N; ++i) s += a[i * N + j];
-    const float r = __frcp_rn(s + eps);
+    const float r = fast_rcp(s + eps);
     float dot = 0.f;
 MHC_UNROLL_N
     for (int i = 0; i < N; ++i) dot += g[i * N + j] * (a[i * N + j] * r);

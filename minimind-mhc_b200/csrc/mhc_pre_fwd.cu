@@ -194,7 +194,7 @@ coef_fwd_kernel(const Tx *__restrict__ x, int64_t T, int nC, const void *__restr
   for (int t = tid; t < TM; t += Cf::THREADS) {
     const int64_t tok = tok0 + t;
     if (tok >= T) continue;
-    const float inv = 1.0f / sqrtf(ssq_s[t] / (float)nC + p.rms_eps);
+    const float inv = rsqrtf(ssq_s[t] / (float)nC + p.rms_eps);
     inv_rms[tok] = inv;
     float m[FD];
     MHC_UNROLL_N
@@ -285,7 +285,7 @@ head1_fwd_kernel(const Tx *__restrict__ x, Tx *__restrict__ out, float *__restri
       ss += v * v;
     }
     ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / (float)C + eps);
+    const float inv = rsqrtf(ss / (float)C + eps);
     if (lane == 0) inv_rms[t] = inv;
     for (int c = lane; c < C; c += 32) out[t * C + c] = from_f<Tx>(to_f(xr[c]) * inv);
   }

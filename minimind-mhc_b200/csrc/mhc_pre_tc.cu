@@ -2,10 +2,14 @@
 //
 // One persistent kernel per call, launched as clusters of S = 8 CTAs (one CTA
 // per SM).  A cluster owns a sequence of 128-token tiles; CTA r of the cluster
-// owns K-slice r of the n*C reduction:
+// owns K-slice r of the n*C reduction, finalises the coefficients of tokens
+// [16r, 16r+16) of every tile and computes z for columns [r*C/8, (r+1)*C/8).
 //
-//   warp 0      TMA producer: 128 x 64 bf16 chunks of its x K-slice into an
-//               8-slot ring (128-byte swizzle, 16 KB per slot).
+//   warp 0 l0   TMA producer: 128 x 64 bf16 chunks of its x K-slice into a
+//               ring (128-byte swizzle, 16 KB per slot).
+//   warp 0 l1   pre-aggregate producer: once every CTA of the cluster has
+//               finished a tile's projection (so the tile's x is in L2), TMA
+//               boxes of 32 tokens x n streams x C/8 columns (3-D tensor map).
 //   warp 1      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
 //               (M = 128, K = 16 per instruction) into a double-buffered TMEM
 //               accumulator.  phi is split once per launch into bf16 hi | lo
@@ -14,20 +18,23 @@
 //   warps 2-5   row warps (thread = token row = TMEM lane): sum of squares of
 //               the slice while the chunks land, then the slice's partial
 //               projection from TMEM; the (FD partials, sum of squares) row is
-//               pushed over DSMEM into the inbox of the CTA that owns that
-//               token's coefficients (16 tokens per CTA).
+//               pushed with st.async into the inbox of the CTA that owns the
+//               token (the stores complete the owner's mbarrier themselves).
 //   warp 6      coefficient warp: sums the 8 slices in a fixed order
 //               (deterministic), applies 1/rms, the sigmoid gates and the
-//               H_res affine map, writes the per-token outputs and pushes the
-//               fp32 aggregation weights to all 8 CTAs.
-//   warps 7-14  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] for this
-//               CTA's C/8 columns, re-reading x from L2 (the cluster fetched it
-//               from HBM microseconds earlier).
+//               H_res affine map, pushes the fp32 aggregation weights to all 8
+//               CTAs with st.async and writes the per-token outputs.
+//   warps 7-8   Sinkhorn warps, alternating tiles: H_res of the CTA's 16
+//               tokens (one token per lane, matrix in registers).  The logits
+//               are 4-deep buffered, so the 20 iterations stay off the tile's
+//               critical path.
+//   warps 9-16  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] from the
+//               staged boxes.
 //
-// All producer / consumer hand-offs are mbarriers (remote ones arrive with
-// release.cluster); there is no named barrier or other unbounded wait inside
-// the tile loop.  Every wait is bounded (mhc_sm100.cuh) and a timeout sets the
-// device error word, drains the CTA's own async work, frees TMEM and exits.
+// All hand-offs are mbarriers.  There is no named barrier, no cluster barrier
+// and no fence inside the tile loop, and every wait is bounded
+// (mhc_sm100.cuh): a timeout sets the device error word, drains the CTA's own
+// asynchronous work, frees TMEM and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -46,15 +53,29 @@ using namespace sm100;
 
 constexpr int S = 8;                 // CTAs per cluster (K split)
 constexpr int TM = 128;              // tokens per tile (UMMA M)
-constexpr int RING = 8;              // x chunk slots
+constexpr int RING_MAX = 8;          // x chunk slots (runtime count <= this)
+constexpr int ZS_MAX = 8;            // pre-aggregate box slots (runtime count <= this)
+constexpr int ZR = 32;               // tokens per pre-aggregate box (a quarter tile)
 constexpr int CHUNK = TM * 128;      // 128 rows x 128 bytes
 constexpr int TPC = TM / S;          // tokens whose coefficients a CTA finalises
-constexpr int NWARPS = 15, NTHREADS = NWARPS * 32;
-constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_Z = 7, NZW = 8;
-constexpr int TMEM_COLS = 128;            // two accumulators of up to 64 columns
-constexpr int ZU = 3;                     // z items in flight per thread
+constexpr int NWARPS = 17, NTHREADS = NWARPS * 32;
+constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_SK = 7, NSK = 2, W_Z = 9, NZW = 8;
+constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
+constexpr int HB = 4;                // weights / logits buffers (tiles in flight after the coefficients)
+constexpr int TMEM_COLS = 128;       // two accumulators of up to 64 columns
 
-enum ErrCode { ERR_PROD = 1, ERR_MMA = 2, ERR_ROW = 3, ERR_COEF = 4, ERR_Z = 5 };
+// Per-tile timeline instrumentation (clock64 of cluster 0, CTA 0), compiled in
+// only with -DMHC_TC_TRACE; events are indexed [local tile][event].
+#ifdef MHC_TC_TRACE
+__device__ long long g_trace[64][32];
+#define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = clock64(); } while (0)
+#else
+#define TC_TRACE(ev) do { } while (0)
+#endif
+enum TraceEv { T_P_FIRST, T_P_LAST, T_M_ACCE, T_M_COMMIT, T_R_FULL0, T_R_ACCF, T_R_INE, T_R_PUSHED, T_C_INF,
+               T_C_HPE, T_C_PUSHED, T_Z_BOX3, T_Z_HPF, T_SK_LGF, T_SK_DONE, T_Z_BOX0, T_Z_DONE, T_ZP_GO, T_C_LGE };
+
+enum ErrCode { ERR_PROD = 1, ERR_MMA = 2, ERR_ROW = 3, ERR_COEF = 4, ERR_Z = 5, ERR_SK = 6 };
 
 template <int N, int MODE>
 struct Cfg {
@@ -66,22 +87,25 @@ struct Cfg {
 };
 
 struct Layout {
-  uint32_t ring, phi, inbox, hp, lg, par, bar, tmem, abort, total;
+  uint32_t ring, phi, zbuf, inbox, hp, lg, par, bar, tmem, abort, total;
 };
 
 // barrier slots
-constexpr int B_FULL = 0, B_EMPTY = RING, B_ACCF = 2 * RING, B_ACCE = 2 * RING + 2, B_INF = 2 * RING + 4,
-              B_INE = 2 * RING + 6, B_HPF = 2 * RING + 8, B_HPE = 2 * RING + 10, B_ZD = 2 * RING + 12,
-              B_DRAIN = 2 * RING + 14, NBARS = 2 * RING + 15;
+constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ZF = 2 * RING_MAX, B_ZE = B_ZF + ZS_MAX, B_ACCF = B_ZE + ZS_MAX,
+              B_ACCE = B_ACCF + 2, B_INF = B_ACCE + 2, B_INE = B_INF + IN_BUFS, B_HPF = B_INE + IN_BUFS,
+              B_HPE = B_HPF + HB, B_ZD = B_HPE + HB, B_ZGO = B_ZD + HB, B_LGF = B_ZGO + HB, B_LGE = B_LGF + HB,
+              B_DRAIN = B_LGE + HB, NBARS = B_DRAIN + 1;
 
-__host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR) {
+__host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR, int RING, int ZS,
+                                              int zbox) {
   Layout L;
   uint32_t o = 0;
-  L.ring = o;  o += RING * CHUNK;
+  L.ring = o;  o += (uint32_t)RING * CHUNK;
   L.phi = o;   o += (uint32_t)CH * NB * 128;
-  L.inbox = o; o += 2u * S * TPC * IBS * 4;
-  L.hp = o;    o += 2u * TM * HPN * 4;
-  L.lg = o;    o += 2u * TPC * 16 * 4;   // H_res logits of the CTA's own tokens (n <= 4)
+  L.zbuf = o;  o += (uint32_t)ZS * zbox;
+  L.inbox = o; o += (uint32_t)IN_BUFS * S * TPC * IBS * 4;
+  L.hp = o;    o += (uint32_t)HB * TM * HPN * 4;
+  L.lg = o;    o += (uint32_t)HB * TPC * 16 * 4;   // H_res logits of the CTA's own tokens (n <= 4)
   L.par = o;   o += ((NPAR * 4 + 15) / 16) * 16;
   L.bar = o;   o += NBARS * 8;
   L.tmem = o;  o += 4;
@@ -93,6 +117,7 @@ __host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, 
 struct Args {
   int64_t T;
   int C, nC, KS, CH;
+  int RING, ZS, zbox;   // x ring slots, pre-aggregate box slots, box bytes
   const void *phi;
   CoefParams p;
   __nv_bfloat16 *z;
@@ -143,16 +168,19 @@ __device__ __forceinline__ void load_params_tc(float *par, const CoefParams &p, 
 
 template <int N, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__restrict__ x, Args a) {
+pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap zmap,
+              const __nv_bfloat16 *__restrict__ x, Args a) {
   using Cf = Cfg<N, MODE>;
   constexpr int FD = Cf::FD, NB = Cf::NB, IBS = Cf::IBS, NPAR = Cf::NPAR, HPN = Cf::HPN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t *base = smem_raw + (base_u32 - raw_u32);
-  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR);
+  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR, a.RING, a.ZS, a.zbox);
+  const int RING = a.RING, ZS = a.ZS;
   float *inbox = reinterpret_cast<float *>(base + L.inbox);
   float *hp = reinterpret_cast<float *>(base + L.hp);
+  float *lg = reinterpret_cast<float *>(base + L.lg);
   float *par = reinterpret_cast<float *>(base + L.par);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(base + L.abort);
   const uint32_t bar0 = base_u32 + L.bar;
@@ -165,6 +193,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
   const uint32_t rank = cluster_ctarank(), cid = cluster_id_x(), ncl = ncluster_x();
   const int ntiles = (int)((a.T + TM - 1) / TM);
   const int CH = a.CH;
+  constexpr uint32_t INBOX_TX = (uint32_t)S * TPC * IBS * 4;   // bytes landing in one inbox buffer
+  constexpr uint32_t HP_TX = (uint32_t)S * TPC * HPN * 4;      // bytes landing in one weights buffer
 
   // ---------------- prologue ----------------
   if (tid == 0) {
@@ -173,14 +203,25 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       mbar_init(BAR(B_FULL + i), 1);
       mbar_init(BAR(B_EMPTY + i), 1 + 4);  // MMA commit + 4 row warps
     }
+    for (int i = 0; i < ZS; ++i) {
+      mbar_init(BAR(B_ZF + i), 1);
+      mbar_init(BAR(B_ZE + i), NZW);       // every pre-aggregate warp
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(B_ACCF + b), 1);
       mbar_init(BAR(B_ACCE + b), 4);
-      mbar_init(BAR(B_INF + b), S);  // one per source CTA (its half-warp of owned rows)
-      mbar_init(BAR(B_INE + b), S);  // one per owner CTA (inbox rows consumed)
-      mbar_init(BAR(B_HPF + b), S);  // one per source CTA (its 16 tokens' weights)
-      mbar_init(BAR(B_HPE + b), S);  // one per CTA's pre-aggregate group
+    }
+    for (int b = 0; b < IN_BUFS; ++b) {
+      mbar_init(BAR(B_INF + b), 1);        // armed by the coefficient warp; st.async bytes complete it
+      mbar_init(BAR(B_INE + b), S);        // one per owner CTA (inbox rows consumed)
+    }
+    for (int b = 0; b < HB; ++b) {
+      mbar_init(BAR(B_HPF + b), 1);        // armed by the pre-aggregate warps; st.async bytes complete it
+      mbar_init(BAR(B_HPE + b), S);        // one per CTA (its pre-aggregate is done)
       mbar_init(BAR(B_ZD + b), NZW);       // local: pre-aggregate warps done
+      mbar_init(BAR(B_ZGO + b), 1);        // local: tile's projections complete cluster-wide
+      mbar_init(BAR(B_LGF + b), 1);        // local: logits of the CTA's tokens written
+      mbar_init(BAR(B_LGE + b), 1);        // local: Sinkhorn warp done with the logits
     }
     mbar_init(BAR(B_DRAIN), 1);
     fence_mbar_init_cluster();
@@ -212,18 +253,21 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
   }
   fence_proxy_async_smem();  // generic phi writes -> tensor-core (async proxy) reads
   __syncthreads();
-  cluster_sync_all();        // every CTA's barriers exist before any remote arrive
+  cluster_sync_all();        // every CTA's barriers exist before any remote arrive or st.async
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
 
   if (warp == W_PROD) {
-    // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // ---------------- x chunk producer ----------------
       uint32_t q = 0;
+      int lt = 0;
       bool ok = true;
-      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl) {
+      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
+          if (c == 0) TC_TRACE(T_P_FIRST);
+          if (c == CH - 1) TC_TRACE(T_P_LAST);
           mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
           tma_load_2d(base_u32 + L.ring + slot * CHUNK, &tmap, (int)rank * a.KS + c * 64, tile * TM,
                       BAR(B_FULL + slot));
@@ -233,6 +277,28 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       // copies in flight must land before the CTA can exit
       const uint32_t q0 = q > (uint32_t)RING ? q - RING : 0u;
       for (uint32_t p = q0; p < q; ++p) wait_parity<false>(BAR(B_FULL + p % RING), (p / RING) & 1u, nullptr);
+    } else if (lane == 1) {
+      // ---------------- pre-aggregate box producer ----------------
+      const int cz = a.C / S;
+      uint32_t zq = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+        const int hb = lt % HB;
+        const uint32_t hph = (uint32_t)(lt / HB) & 1u;
+        if (!wait_parity<false>(BAR(B_ZGO + hb), hph, abort_flag)) { ok = false; break; }
+        TC_TRACE(T_ZP_GO);
+        for (int qq = 0; qq < TM / ZR; ++qq, ++zq) {
+          const uint32_t slot = zq % ZS, zph = (zq / ZS) & 1u;
+          if (!wait_parity<false>(BAR(B_ZE + slot), zph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR(B_ZF + slot), (uint32_t)a.zbox);
+          tma_load_3d(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0, tile * TM + qq * ZR,
+                      BAR(B_ZF + slot));
+        }
+      }
+      if (!ok) record_error(ERR_PROD, abort_flag);
+      const uint32_t q0 = zq > (uint32_t)ZS ? zq - ZS : 0u;
+      for (uint32_t p = q0; p < zq; ++p) wait_parity<false>(BAR(B_ZF + p % ZS), (p / ZS) & 1u, nullptr);
     }
     __syncwarp();
   } else if (warp == W_MMA) {
@@ -246,6 +312,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         const int buf = lt & 1;
         const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
         if (!wait_parity<false>(BAR(B_ACCE + buf), aph ^ 1u, abort_flag)) { ok = false; break; }
+        TC_TRACE(T_M_ACCE);
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)buf * 64u;
         for (int c = 0; c < CH; ++c, ++q) {
@@ -262,6 +329,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         }
         if (!ok) break;
         umma_commit(BAR(B_ACCF + buf));
+        TC_TRACE(T_M_COMMIT);
       }
       if (!ok) record_error(ERR_MMA, abort_flag);
       // every issued MMA completes before TMEM is released
@@ -273,6 +341,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
     // ---------------- row warps ----------------
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;     // token row of the tile = TMEM lane
+    const uint32_t owner = (uint32_t)(row / TPC);
     uint32_t q = 0;
     int lt = 0;
     bool ok = true;
@@ -281,6 +350,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       for (int c = 0; c < CH; ++c, ++q) {
         const uint32_t slot = q % RING, ph = (q / RING) & 1u;
         if (!WAIT_WARP(false, BAR(B_FULL + slot), ph)) { ok = false; break; }
+        if (c == 0 && warp == W_ROW && lane == 0) TC_TRACE(T_R_FULL0);
         const uint8_t *rp = base + L.ring + slot * CHUNK + row * 128;
 #pragma unroll
         for (int u = 0; u < 8; ++u) ss += sq8(*reinterpret_cast<const uint4 *>(rp + ((u ^ (row & 7)) << 4)));
@@ -292,6 +362,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       const int buf = lt & 1;
       const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
       if (!WAIT_WARP(false, BAR(B_ACCF + buf), aph)) { ok = false; break; }
+      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_ACCF);
       tc_fence_after();
       float d[NB];
 #pragma unroll
@@ -310,43 +381,42 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
 #pragma unroll
       for (int j = 0; j < FD; ++j) vals[j] = d[j] + d[FD + j];
       vals[FD] = ss;
-      // the owner's inbox slot for this buffer must have been drained
-      if (!WAIT_WARP(true, BAR(B_INE + buf), aph ^ 1u)) { ok = false; break; }
-      const uint32_t owner = (uint32_t)(row / TPC);
-      const uint32_t dst = mapa(base_u32 + L.inbox + (uint32_t)(((buf * S + (int)rank) * TPC + (row % TPC)) * IBS * 4),
+      // the owners' inbox buffer must have been drained (tile lt - IN_BUFS)
+      const int ib = lt % IN_BUFS;
+      if (!WAIT_WARP(true, BAR(B_INE + ib), ((uint32_t)(lt / IN_BUFS) & 1u) ^ 1u)) { ok = false; break; }
+      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_INE);
+      const uint32_t dst = mapa(base_u32 + L.inbox + (uint32_t)(((ib * S + (int)rank) * TPC + (row % TPC)) * IBS * 4),
                                 owner);
+      const uint32_t dbar = mapa(BAR(B_INF + ib), owner);
 #pragma unroll
       for (int v = 0; v < IBS / 4; ++v)
-        st_cluster_v4(dst + v * 16, vals[4 * v], vals[4 * v + 1], vals[4 * v + 2], vals[4 * v + 3]);
-      // publish: every lane fences its own stores at cluster scope, then one
-      // lane per half-warp (16 rows = one owner) arrives with release
-      fence_acq_rel_cluster();
-      __syncwarp();
-      if ((lane & 15) == 0) mbar_arrive_cluster(mapa(BAR(B_INF + buf), owner));
+        st_async_v4(dst + v * 16, vals[4 * v], vals[4 * v + 1], vals[4 * v + 2], vals[4 * v + 3], dbar);
+      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_PUSHED);
     }
     if (!ok) record_error(ERR_ROW, abort_flag);
   } else if (warp == W_COEF) {
     // ---------------- coefficient warp ----------------
-    float *lg = reinterpret_cast<float *>(base + L.lg);
     int lt = 0;
     bool ok = true;
     for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
-      const int buf = lt & 1;
-      const uint32_t ph = (uint32_t)(lt >> 1) & 1u;
-      if (!WAIT_WARP(true, BAR(B_INF + buf), ph)) { ok = false; break; }
+      const int ib = lt % IN_BUFS, hb = lt % HB;
+      const uint32_t iph = (uint32_t)(lt / IN_BUFS) & 1u, hph = (uint32_t)(lt / HB) & 1u;
+      if (lane == 0) mbar_arrive_expect_tx(BAR(B_INF + ib), INBOX_TX);  // arm: all 8 slices' rows
+      if (!WAIT_WARP(true, BAR(B_INF + ib), iph)) { ok = false; break; }
+      if (lane == 0) TC_TRACE(T_C_INF);
       float acc[FD + 1];
 #pragma unroll
       for (int j = 0; j <= FD; ++j) acc[j] = 0.f;
       if (lane < TPC) {
 #pragma unroll 1
         for (int s = 0; s < S; ++s) {  // fixed order over the K slices: deterministic
-          const float *src = inbox + ((buf * S + s) * TPC + lane) * IBS;
+          const float *src = inbox + ((ib * S + s) * TPC + lane) * IBS;
 #pragma unroll
           for (int j = 0; j <= FD; ++j) acc[j] += src[j];
         }
       }
       __syncwarp();
-      if (lane < S) mbar_arrive_remote(mapa(BAR(B_INE + buf), (uint32_t)lane));  // inbox rows free again
+      if (lane < S) mbar_arrive_remote(mapa(BAR(B_INE + ib), (uint32_t)lane));  // inbox rows free again
       const int t = (int)rank * TPC + lane;  // token row of the tile
       const int64_t tok = (int64_t)tile * TM + t;
       const bool live = lane < TPC && tok < a.T;
@@ -354,10 +424,20 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       float inv = 0.f;
 #pragma unroll
       for (int i = 0; i < HPN; ++i) w[i] = 0.f;
-      // this CTA's weights and logits buffers of `buf` must be free (pre-aggregate of tile lt-2 done)
-      if (!WAIT_WARP(true, BAR(B_HPE + buf), ph ^ 1u)) { ok = false; break; }
+      // the weights buffer `hb` must be free in every CTA (tile lt-HB done everywhere)
+      if (!WAIT_WARP(true, BAR(B_HPE + hb), hph ^ 1u)) { ok = false; break; }
+      if (lane == 0) TC_TRACE(T_C_HPE);
+      // every CTA finished this tile's projection, so its x is in L2: start the
+      // pre-aggregate loads.  Signalled only after tile lt-HB is done everywhere,
+      // so the box producer never sees two phases of ZGO[hb] at once.
+      if (lane == 0) mbar_arrive(BAR(B_ZGO + hb));
+      // and the logits buffer must be free (Sinkhorn of tile lt-HB done)
+      if constexpr (MODE == FULL) {
+        if (!WAIT_WARP(false, BAR(B_LGE + hb), hph ^ 1u)) { ok = false; break; }
+        if (lane == 0) TC_TRACE(T_C_LGE);
+      }
       if (lane < TPC) {
-        inv = 1.0f / sqrtf(acc[FD] / (float)a.nC + a.p.rms_eps);
+        inv = rsqrtf(acc[FD] / (float)a.nC + a.p.rms_eps);
 #pragma unroll
         for (int j = 0; j < FD; ++j) m[j] = acc[j] * inv;
 #pragma unroll
@@ -367,23 +447,27 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
             ho[i] = sigmoidf_(__fadd_rn(__fmul_rn(m[N + i], par[1]), par[3 + N + i])) * a.p.post_mult;
         }
         if constexpr (MODE == FULL) {
-          float *lrow = lg + (buf * TPC + lane) * 16;
+          float *lrow = lg + (hb * TPC + lane) * 16;
 #pragma unroll
           for (int k = 0; k < N * N; ++k) lrow[k] = __fadd_rn(__fmul_rn(m[2 * N + k], par[2]), par[3 + 2 * N + k]);
         }
         // publish the aggregation weights to every CTA of the cluster
-        const uint32_t loc = base_u32 + L.hp + (uint32_t)((buf * TM + t) * HPN * 4);
+        const uint32_t loc = base_u32 + L.hp + (uint32_t)((hb * TM + t) * HPN * 4);
 #pragma unroll 1
         for (int dcta = 0; dcta < S; ++dcta) {
           const uint32_t dst = mapa(loc, (uint32_t)dcta);
+          const uint32_t dbar = mapa(BAR(B_HPF + hb), (uint32_t)dcta);
 #pragma unroll
-          for (int v = 0; v < HPN / 4; ++v) st_cluster_v4(dst + v * 16, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          for (int v = 0; v < HPN / 4; ++v)
+            st_async_v4(dst + v * 16, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3], dbar);
         }
       }
-      fence_acq_rel_cluster();
-      __syncwarp();
-      if (lane < S) mbar_arrive_cluster(mapa(BAR(B_HPF + buf), (uint32_t)lane));
-      // per-token outputs (after the hand-off so they do not delay it)
+      if (lane == 0) TC_TRACE(T_C_PUSHED);
+      if constexpr (MODE == FULL) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(B_LGF + hb));  // logits ready for the Sinkhorn warp
+      }
+      // per-token outputs
       if (live) {
         a.inv_rms[tok] = inv;
 #pragma unroll
@@ -398,111 +482,103 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       }
     }
     if (!ok) record_error(ERR_COEF, abort_flag);
+  } else if (warp < W_SK + NSK) {
+    // ---------------- Sinkhorn warps: H_res of the CTA's 16 tokens ----------------
+    // (idle when the layer has no H_res segment)
+    if constexpr (MODE == FULL) {
+      const int wsk = warp - W_SK;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+        if (lt % NSK != wsk) continue;
+        const int hb = lt % HB;
+        const uint32_t hph = (uint32_t)(lt / HB) & 1u;
+        if (!WAIT_WARP(false, BAR(B_LGF + hb), hph)) { ok = false; break; }
+        if (lane == 0) TC_TRACE(T_SK_LGF);
+        const int64_t tok = (int64_t)tile * TM + (int)rank * TPC + lane;
+        if (lane < TPC && tok < a.T) {
+          float hm[N * N];
+#pragma unroll
+          for (int k = 0; k < N * N; ++k) hm[k] = lg[(hb * TPC + lane) * 16 + k];
+          if (a.p.apply_sinkhorn) sinkhorn_fwd<N>(hm, a.p.sk_iters, a.p.sk_eps);
+          if (a.h_res) {
+#pragma unroll
+            for (int k = 0; k < N * N; ++k) store_dyn(a.h_res, a.coef_dtype, tok * N * N + k, hm[k]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) TC_TRACE(T_SK_DONE);
+        if (lane == 0) mbar_arrive(BAR(B_LGE + hb));  // logits buffer free
+      }
+      if (!ok) record_error(ERR_SK, abort_flag);
+    }
   } else {
-    // ---------------- pre-aggregate warps (+ Sinkhorn of the CTA's own tokens) ----------------
-    const float *lg = reinterpret_cast<const float *>(base + L.lg);
+    // ---------------- pre-aggregate warps ----------------
     const int ztid = tid - W_Z * 32;
     const int cz = a.C / S;      // columns of z owned by this CTA
-    const int vpr = cz / 8;      // 16-byte vectors per row
+    const int vpr = cz / 8;      // 16-byte vectors per row and stream
     const int c0 = (int)rank * cz;
-    const int items = TM * vpr;
-    constexpr int NN = N * N;    // threads per token in the Sinkhorn step
+    const int zrow = N * cz * 2; // bytes per box token (N streams x cz columns)
+    const int qitems = ZR * vpr;
+    uint32_t zq = 0;             // boxes consumed so far
     int lt = 0;
     bool ok = true;
     for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
-      const int buf = lt & 1;
-      const uint32_t ph = (uint32_t)(lt >> 1) & 1u;
-      if (!WAIT_WARP(true, BAR(B_HPF + buf), ph)) { ok = false; break; }
-      const float *hps = hp + buf * TM * HPN;
-      uint4 raw[ZU][N];
-      auto load_round = [&](int it0) {
-#pragma unroll
-        for (int u = 0; u < ZU; ++u) {
-          const int it = it0 + u * NZW * 32;
-          const int t = it / vpr;
+      const int hb = lt % HB;
+      const uint32_t hph = (uint32_t)(lt / HB) & 1u;
+      if (warp == W_Z && lane == 0) mbar_arrive_expect_tx(BAR(B_HPF + hb), HP_TX);  // arm: 8 CTAs' weights
+      if (!WAIT_WARP(true, BAR(B_HPF + hb), hph)) { ok = false; break; }
+      if (warp == W_Z && lane == 0) TC_TRACE(T_Z_HPF);
+      const float *hps = hp + hb * TM * HPN;
+      for (int qq = 0; qq < TM / ZR; ++qq, ++zq) {
+        const uint32_t slot = zq % ZS;
+        if (!WAIT_WARP(false, BAR(B_ZF + slot), (zq / ZS) & 1u)) { ok = false; break; }
+        if (warp == W_Z && lane == 0 && qq == 0) TC_TRACE(T_Z_BOX0);
+        if (warp == W_Z && lane == 0 && qq == TM / ZR - 1) TC_TRACE(T_Z_BOX3);
+        const uint8_t *box = base + L.zbuf + slot * (uint32_t)a.zbox;
+        for (int it = ztid; it < qitems; it += NZW * 32) {
+          const int r = it / vpr, v = it - r * vpr;
+          const int t = qq * ZR + r;
           const int64_t tk = (int64_t)tile * TM + t;
-          if (it < items && tk < a.T) {
-            const __nv_bfloat16 *xr = x + tk * a.nC + c0 + (it - t * vpr) * 8;
+          if (tk >= a.T) continue;
+          float acc[8];
 #pragma unroll
-            for (int i = 0; i < N; ++i) raw[u][i] = __ldcs(reinterpret_cast<const uint4 *>(xr + (int64_t)i * a.C));
+          for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+          float wv[HPN];
+#pragma unroll
+          for (int v4 = 0; v4 < HPN / 4; ++v4) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(hps + t * HPN + 4 * v4);
+            wv[4 * v4] = q4.x; wv[4 * v4 + 1] = q4.y; wv[4 * v4 + 2] = q4.z; wv[4 * v4 + 3] = q4.w;
           }
-        }
-      };
-      auto consume_round = [&](int it0) {
 #pragma unroll
-        for (int u = 0; u < ZU; ++u) {
-          const int it = it0 + u * NZW * 32;
-          const int t = it / vpr;
-          const int v = it - t * vpr;
-          const int64_t tk = (int64_t)tile * TM + t;
-          if (it < items && tk < a.T) {
-            float acc[8];
+          for (int st = 0; st < N; ++st) {
+            const float wi = wv[st];
+            Pack<__nv_bfloat16> pk;
+            pk.raw = *reinterpret_cast<const uint4 *>(box + r * zrow + st * cz * 2 + v * 16);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll
-            for (int i = 0; i < N; ++i) {
-              const float wi = hps[t * HPN + i];
-              Pack<__nv_bfloat16> pk;
-              pk.raw = raw[u][i];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc[e] = fmaf(wi, pk.get(e), acc[e]);
-            }
-            Pack<__nv_bfloat16> o;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o.set(e, acc[e]);
-            *reinterpret_cast<uint4 *>(a.z + tk * a.C + c0 + v * 8) = o.raw;
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(wi, pk.get(e), acc[e]);
           }
+          Pack<__nv_bfloat16> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.set(e, acc[e]);
+          *reinterpret_cast<uint4 *>(a.z + tk * a.C + c0 + v * 8) = o.raw;
         }
-      };
-      load_round(ztid);
-      if constexpr (MODE == FULL) {
-        // while the first loads are in flight: H_res of the CTA's 16 tokens, one
-        // matrix element per thread, row / column sums over lane shuffles (all
-        // 256 threads take part so every shuffle has a full warp)
-        const int sk_t = ztid / NN, e = ztid % NN;
-        const bool sk_live = sk_t < TPC;
-        float v = sk_live ? lg[(buf * TPC + sk_t) * 16 + e] : 0.f;
-        if (a.p.apply_sinkhorn) {
-          float mx = v;
-#pragma unroll
-          for (int o = 1; o < N; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          const float ex = expf(v - mx);
-          float rs = ex;
-#pragma unroll
-          for (int o = 1; o < N; o <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
-          v = ex * (1.0f / rs) + a.p.sk_eps;
-          float cs = v;
-#pragma unroll
-          for (int o = N; o < NN; o <<= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-          v = v * (1.0f / (cs + a.p.sk_eps));
-          for (int itr = 1; itr < a.p.sk_iters; ++itr) {
-            float r = v;
-#pragma unroll
-            for (int o = 1; o < N; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-            v = v * (1.0f / (r + a.p.sk_eps));
-            float c = v;
-#pragma unroll
-            for (int o = N; o < NN; o <<= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-            v = v * (1.0f / (c + a.p.sk_eps));
-          }
-        }
-        const int64_t sk_tok = (int64_t)tile * TM + (int)rank * TPC + sk_t;
-        if (sk_live && sk_tok < a.T && a.h_res) store_dyn(a.h_res, a.coef_dtype, sk_tok * NN + e, v);
+        // the box may be refilled
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(B_ZE + slot));
       }
-      consume_round(ztid);
-      for (int it0 = ztid + ZU * NZW * 32; it0 < items; it0 += ZU * NZW * 32) {
-        load_round(it0);
-        consume_round(it0);
-      }
-      // this CTA is done reading the weights / logits of `buf`: tell every writer
+      if (!ok) break;
+      // this CTA is done reading the weights of `hb`: tell every writer
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(B_ZD + buf));
+      if (lane == 0) mbar_arrive(BAR(B_ZD + hb));
       if (warp == W_Z) {
         int good = 1;
         if (lane == 0) {
-          good = wait_parity<false>(BAR(B_ZD + buf), ph, abort_flag) ? 1 : 0;
+          good = wait_parity<false>(BAR(B_ZD + hb), hph, abort_flag) ? 1 : 0;
+          TC_TRACE(T_Z_DONE);
           if (good)
-            for (int s = 0; s < S; ++s) mbar_arrive_remote(mapa(BAR(B_HPE + buf), (uint32_t)s));
+            for (int s = 0; s < S; ++s) mbar_arrive_remote(mapa(BAR(B_HPE + hb), (uint32_t)s));
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
       }
@@ -538,27 +614,67 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block on sm_100
+
+// Ring / box slot counts that fit the shared-memory budget.
 template <int N, int MODE>
-static cudaError_t launch_impl(const void *x, int64_t T, int C, const Args &args, cudaStream_t stream) {
+static bool pick_slots(int CH, int zbox, int &ring, int &zs) {
+  using Cf = Cfg<N, MODE>;
+  // (x chunks, quarter-tile boxes) in flight, in order of preference
+#if defined(MHC_TC_RING) && defined(MHC_TC_ZS)
+  const int prefs[][2] = {{MHC_TC_RING, MHC_TC_ZS}};
+#else
+  const int prefs[][2] = {{5, 3}, {4, 4}, {6, 2}, {4, 3}, {4, 2}, {3, 2}};
+#endif
+  for (const auto &pr : prefs) {
+    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, pr[0], pr[1], zbox);
+    if ((size_t)L.total + 1024 <= SMEM_LIMIT) {
+      ring = pr[0];
+      zs = pr[1];
+      return true;
+    }
+  }
+  return false;
+}
+
+template <int N, int MODE>
+static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaStream_t stream) {
   using Cf = Cfg<N, MODE>;
   const int nC = N * C;
-  const Layout L = make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR);
+  args.zbox = ZR * N * (C / S) * 2;
+  if (!pick_slots<N, MODE>(args.CH, args.zbox, args.RING, args.ZS)) return cudaErrorNotSupported;
+  const Layout L = make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox);
   const size_t smem = (size_t)L.total + 1024;
   auto kern = pre_tc_kernel<N, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tmap;
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
-  const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)TM};
-  const cuuint32_t estr[2] = {1, 1};
-  if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorNotSupported;
+  // x as (T rows) x (nC columns): 128-row x 64-column K chunks, 128-byte swizzle
+  CUtensorMap tmap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)TM};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorNotSupported;
+  }
+  // x as (T) x (n streams) x (C columns): boxes of ZR tokens x n streams x C/8 columns
+  CUtensorMap zmap;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)N, (cuuint64_t)T};
+    const cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)nC * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)(C / S), (cuuint32_t)N, (cuuint32_t)ZR};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(&zmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorNotSupported;
+  }
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -587,7 +703,7 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, const Args &args
   const int64_t ntiles = (T + TM - 1) / TM;
   const int clusters = (int)(ntiles < mc ? ntiles : mc);
   cfg.gridDim = dim3((unsigned)(clusters * S), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, zmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -604,6 +720,7 @@ bool pre_tc_eligible(int mode, int n, int x_dtype, const void *x, const void *z,
   const int64_t nC = (int64_t)n * C;
   if (nC % (tc::S * 64) != 0 || C % (tc::S * 8) != 0) return false;
   if (nC / tc::S / 64 > 8) return false;  // phi slice budget
+  if (C / tc::S > 256) return false;       // TMA box width
   if (((uintptr_t)x & 15) != 0 || ((uintptr_t)z & 15) != 0) return false;
   return true;
 }
@@ -617,6 +734,9 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
   a.nC = n * C;
   a.KS = n * C / tc::S;
   a.CH = a.KS / 64;
+  a.RING = 0;
+  a.ZS = 0;
+  a.zbox = 0;
   a.phi = phi;
   a.p = p;
   a.z = reinterpret_cast<__nv_bfloat16 *>(z);
@@ -630,7 +750,7 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
     constexpr int MODE = decltype(md)::value;
     switch (n) {
       case 1: if constexpr (MODE == FULL) return tc::launch_impl<1, MODE>(x, T, C, a, stream); break;
-      case 2: if constexpr (MODE != HEAD || true) return tc::launch_impl<2, MODE>(x, T, C, a, stream); break;
+      case 2: return tc::launch_impl<2, MODE>(x, T, C, a, stream);
       case 4: return tc::launch_impl<4, MODE>(x, T, C, a, stream);
       case 8: if constexpr (MODE != FULL) return tc::launch_impl<8, MODE>(x, T, C, a, stream); break;
       default: break;
