@@ -139,7 +139,7 @@ __device__ __forceinline__ float fast_rcp(float x) {
   return r;
 }
 
-__device__ __forceinline__ float sigmoidf_(float v) { return fast_rcp(1.0f + expf(-v)); }
+__device__ __forceinline__ float sigmoidf_(float v) { return fast_rcp(1.0f + __expf(-v)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -191,7 +191,7 @@ MHC_UNROLL_N
     float s = 0.f;
 MHC_UNROLL_N
     for (int j = 0; j < N; ++j) {
-      const float e = expf(p[i * N + j] - mx);
+      const float e = __expf(p[i * N + j] - mx);
       p[i * N + j] = e;
       s += e;
     }

@@ -5,34 +5,37 @@
 // owns K-slice r of the n*C reduction, finalises the coefficients of tokens
 // [16r, 16r+16) of every tile and computes z for columns [r*C/8, (r+1)*C/8).
 //
-//   warp 0 l0   TMA producer: 128 x 64 bf16 chunks of its x K-slice into a
+//   warp 0      TMA producer: 128 x 64 bf16 chunks of its x K-slice into a
 //               ring (128-byte swizzle, 16 KB per slot).
-//   warp 0 l1   pre-aggregate producer: once every CTA of the cluster has
+//   warp 1      pre-aggregate producer: once every CTA of the cluster has
 //               finished a tile's projection (so the tile's x is in L2), TMA
 //               boxes of 32 tokens x n streams x C/8 columns (3-D tensor map).
-//   warp 1      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
+//   warp 2      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
 //               (M = 128, K = 16 per instruction) into a double-buffered TMEM
 //               accumulator.  phi is split once per launch into bf16 hi | lo
 //               halves (NB = 2*FD padded to 16) held in shared memory for the
-//               whole launch, so the projection is accurate to ~2^-17.
-//   warps 2-5   row warps (thread = token row = TMEM lane): sum of squares of
-//               the slice while the chunks land, then the slice's partial
-//               projection from TMEM; the (FD partials, sum of squares) row is
-//               pushed with st.async into the inbox of the CTA that owns the
-//               token (the stores complete the owner's mbarrier themselves).
-//   warp 6      coefficient warp: sums the 8 slices in a fixed order
+//               whole launch, so the projection is accurate to ~2^-17.  The
+//               same chunk is also multiplied by itself (G += x . x^T, N = 128):
+//               the diagonal of G is each row's sum of squares, so no thread
+//               reads the x ring and a slot is free as soon as its MMAs retire.
+//   warps 3-6   row warps (thread = token row = TMEM lane): the slice's
+//               partial projection and sum of squares from TMEM; the (FD
+//               partials, sum of squares) row is pushed with st.async into the
+//               inbox of the CTA that owns the token (the stores complete the
+//               owner's mbarrier themselves).
+//   warp 7      coefficient warp: sums the 8 slices in a fixed order
 //               (deterministic), applies 1/rms, the sigmoid gates and the
 //               H_res affine map, pushes the fp32 aggregation weights to all 8
 //               CTAs with st.async and writes the per-token outputs.
-//   warps 7-8   Sinkhorn warps, alternating tiles: H_res of the CTA's 16
-//               tokens (one token per lane, matrix in registers).  The logits
+//   warp 8      Sinkhorn warp: H_res of the CTA's 16 tokens of two tiles at
+//               a time (one token per lane, matrix in registers).  The logits
 //               are 4-deep buffered, so the 20 iterations stay off the tile's
 //               critical path.
 //   warps 9-16  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] from the
-//               staged boxes.
+//               staged boxes, fp32 accumulation in packed pairs.
 //
 // All hand-offs are mbarriers.  There is no named barrier, no cluster barrier
-// and no fence inside the tile loop, and every wait is bounded
+// and no cluster-scope fence inside the tile loop, and every wait is bounded
 // (mhc_sm100.cuh): a timeout sets the device error word, drains the CTA's own
 // asynchronous work, frees TMEM and exits.
 #include <cuda.h>
@@ -59,18 +62,34 @@ constexpr int ZR = 32;               // tokens per pre-aggregate box (a quarter 
 constexpr int CHUNK = TM * 128;      // 128 rows x 128 bytes
 constexpr int TPC = TM / S;          // tokens whose coefficients a CTA finalises
 constexpr int NWARPS = 17, NTHREADS = NWARPS * 32;
-constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_SK = 7, NSK = 2, W_Z = 9, NZW = 8;
+// Each producer / issuer has a warp of its own: a lane that waits on an
+// mbarrier holds up every other branch of its warp.
+constexpr int W_PROD = 0, W_ZPROD = 1, W_MMA = 2, W_ROW = 3, W_COEF = 7, W_SK = 8, W_Z = 9, NZW = 8;
 constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
 constexpr int HB = 4;                // weights / logits buffers (tiles in flight after the coefficients)
-constexpr int TMEM_COLS = 128;       // two accumulators of up to 64 columns
+// TMEM per accumulator buffer: projection (NB <= 64 columns) at +0, the Gram
+// block x . x^T of the chunk rows (128 columns) at +64; two buffers.
+constexpr int ACC_STRIDE = 256, GRAM_OFF = 64, TMEM_COLS = 512;
 
 // Per-tile timeline instrumentation (clock64 of cluster 0, CTA 0), compiled in
 // only with -DMHC_TC_TRACE; events are indexed [local tile][event].
 #ifdef MHC_TC_TRACE
 __device__ long long g_trace[64][32];
 #define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = clock64(); } while (0)
+__device__ long long g_trace_ch[64][8][8];
+#define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = clock64(); } while (0)
+// global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
+__device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TC_MARK(i) do { if (threadIdx.x == 0) { if ((i) == 0) atomicMin(&g_trace_ns[0], gtimer()); else atomicMax(&g_trace_ns[i], gtimer()); } } while (0)
 #else
+#define TC_MARK(i) do { } while (0)
 #define TC_TRACE(ev) do { } while (0)
+#define TC_TRACE_CH(c, k) do { } while (0)
 #endif
 enum TraceEv { T_P_FIRST, T_P_LAST, T_M_ACCE, T_M_COMMIT, T_R_FULL0, T_R_ACCF, T_R_INE, T_R_PUSHED, T_C_INF,
                T_C_HPE, T_C_PUSHED, T_Z_BOX3, T_Z_HPF, T_SK_LGF, T_SK_DONE, T_Z_BOX0, T_Z_DONE, T_ZP_GO, T_C_LGE };
@@ -94,7 +113,10 @@ struct Layout {
 constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ZF = 2 * RING_MAX, B_ZE = B_ZF + ZS_MAX, B_ACCF = B_ZE + ZS_MAX,
               B_ACCE = B_ACCF + 2, B_INF = B_ACCE + 2, B_INE = B_INF + IN_BUFS, B_HPF = B_INE + IN_BUFS,
               B_HPE = B_HPF + HB, B_ZD = B_HPE + HB, B_ZGO = B_ZD + HB, B_LGF = B_ZGO + HB, B_LGE = B_LGF + HB,
-              B_DRAIN = B_LGE + HB, NBARS = B_DRAIN + 1;
+              B_DRAIN = B_LGE + HB, B_PHI = B_DRAIN + 1, NBARS = B_PHI + 1;
+// warps that convert phi / load the parameters in the prologue (all but the
+// producers and the MMA issuer, which start streaming x at once)
+constexpr int W_CONV = W_MMA + 1, NCONV = NWARPS - W_CONV;
 
 __host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR, int RING, int ZS,
                                               int zbox) {
@@ -138,18 +160,6 @@ __device__ __forceinline__ void record_error(int code, volatile int *abort_flag)
   atomicCAS(&g_tc_error, 0, code);
 }
 
-__device__ __forceinline__ float sq8(uint4 v) {
-  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    s = fmaf(f.x, f.x, s);
-    s = fmaf(f.y, f.y, s);
-  }
-  return s;
-}
-
 template <int N, int MODE>
 __device__ __forceinline__ void load_params_tc(float *par, const CoefParams &p, int tid, int nthreads) {
   constexpr int NPAR = 3 + 2 * N + N * N;
@@ -189,6 +199,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
 // agrees on the outcome so it always leaves a loop together
 #define WAIT_WARP(CL, bar, par) (__all_sync(0xffffffffu, wait_parity<CL>((bar), (par), abort_flag)))
 
+  TC_MARK(0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_ctarank(), cid = cluster_id_x(), ncl = ncluster_x();
   const int ntiles = (int)((a.T + TM - 1) / TM);
@@ -201,7 +212,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     *abort_flag = 0;
     for (int i = 0; i < RING; ++i) {
       mbar_init(BAR(B_FULL + i), 1);
-      mbar_init(BAR(B_EMPTY + i), 1 + 4);  // MMA commit + 4 row warps
+      mbar_init(BAR(B_EMPTY + i), 1);      // MMA commit
     }
     for (int i = 0; i < ZS; ++i) {
       mbar_init(BAR(B_ZF + i), 1);
@@ -224,37 +235,58 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       mbar_init(BAR(B_LGE + b), 1);        // local: Sinkhorn warp done with the logits
     }
     mbar_init(BAR(B_DRAIN), 1);
+    mbar_init(BAR(B_PHI), NCONV);
     fence_mbar_init_cluster();
   }
   if (warp == W_MMA) {
     tmem_alloc(base_u32 + L.tmem, TMEM_COLS);
     tmem_relinquish();
   }
-  {
-    // phi slice of this CTA -> bf16 hi | lo, K-major, 128-byte swizzle
-    const int k0 = (int)rank * a.KS;
+  __syncthreads();
+  cluster_sync_all();        // every CTA's barriers exist before any remote arrive or st.async
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
+  if (warp >= W_CONV) {
+    // phi slice of this CTA -> bf16 hi | lo, K-major, 128-byte swizzle, while
+    // the producer already streams the first x chunks.  Loads are batched 8
+    // deep so their latencies overlap.
+    const int ctid = tid - W_CONV * 32, nconv = NCONV * 32;
+    const int k0 = (int)rank * a.KS, total = a.KS * FD;
     uint8_t *phs = base + L.phi;
-    for (int e = tid; e < a.KS * FD; e += NTHREADS) {
-      const int k = e / FD, j = e - k * FD;
-      const float v = load_dyn(a.phi, a.p.param_dtype, (int64_t)(k0 + k) * FD + j);
-      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-      const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-      *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = hi;
-      *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j + FD, k, NB)) = lo;
+    for (int e0 = ctid; e0 < total; e0 += 8 * nconv) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * nconv;
+        if (e < total) {
+          const int k = e / FD, j = e - k * FD;
+          v[u] = load_dyn(a.phi, a.p.param_dtype, (int64_t)(k0 + k) * FD + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * nconv;
+        if (e < total) {
+          const int k = e / FD, j = e - k * FD;
+          const __nv_bfloat16 hi = __float2bfloat16_rn(v[u]);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(v[u] - __bfloat162float(hi));
+          *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = hi;
+          *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j + FD, k, NB)) = lo;
+        }
+      }
     }
     constexpr int PADR = NB - 2 * FD;
     if constexpr (PADR > 0) {
-      for (int e = tid; e < a.KS * PADR; e += NTHREADS) {
+      for (int e = ctid; e < a.KS * PADR; e += nconv) {
         const int k = e / PADR, j = 2 * FD + (e - (e / PADR) * PADR);
         *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = __float2bfloat16_rn(0.f);
       }
     }
-    load_params_tc<N, MODE>(par, a.p, tid, NTHREADS);
+    load_params_tc<N, MODE>(par, a.p, ctid, nconv);
+    fence_proxy_async_smem();  // generic phi writes -> tensor-core (async proxy) reads
+    __syncwarp();
+    if (lane == 0) mbar_arrive(BAR(B_PHI));
   }
-  fence_proxy_async_smem();  // generic phi writes -> tensor-core (async proxy) reads
-  __syncthreads();
-  cluster_sync_all();        // every CTA's barriers exist before any remote arrive or st.async
-  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
+  TC_MARK(1);
 
   if (warp == W_PROD) {
     if (lane == 0) {
@@ -266,6 +298,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
+          TC_TRACE_CH(c, 0);
           if (c == 0) TC_TRACE(T_P_FIRST);
           if (c == CH - 1) TC_TRACE(T_P_LAST);
           mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
@@ -277,7 +310,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       // copies in flight must land before the CTA can exit
       const uint32_t q0 = q > (uint32_t)RING ? q - RING : 0u;
       for (uint32_t p = q0; p < q; ++p) wait_parity<false>(BAR(B_FULL + p % RING), (p / RING) & 1u, nullptr);
-    } else if (lane == 1) {
+    }
+    __syncwarp();
+  } else if (warp == W_ZPROD) {
+    if (lane == 0) {
       // ---------------- pre-aggregate box producer ----------------
       const int cz = a.C / S;
       uint32_t zq = 0;
@@ -305,26 +341,32 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     // ---------------- tcgen05 MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_f32(128, NB);
+      constexpr uint32_t gdesc = umma_idesc_bf16_f32(128, 128);
       uint32_t q = 0;
       int lt = 0;
-      bool ok = true;
+      bool ok = wait_parity<false>(BAR(B_PHI), 0u, abort_flag);  // phi slice converted
       for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
         const int buf = lt & 1;
         const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
         if (!wait_parity<false>(BAR(B_ACCE + buf), aph ^ 1u, abort_flag)) { ok = false; break; }
         TC_TRACE(T_M_ACCE);
         tc_fence_after();
-        const uint32_t dcol = tmem_base + (uint32_t)buf * 64u;
+        const uint32_t dcol = tmem_base + (uint32_t)buf * ACC_STRIDE;
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_FULL + slot), ph, abort_flag)) { ok = false; break; }
+          TC_TRACE_CH(c, 1);
           tc_fence_after();
           const uint32_t a0 = base_u32 + L.ring + slot * CHUNK;
           const uint32_t b0 = base_u32 + L.phi + (uint32_t)c * NB * 128u;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(dcol, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
-                      (c | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * 32);
+            umma_bf16(dcol, ad, umma_desc_sw128(b0 + k * 32), idesc, (c | k) != 0 ? 1u : 0u);
+            // sum of squares of each row = diagonal of x . x^T: the chunk is
+            // its own B operand (same K-major 128 x 64 layout)
+            umma_bf16(dcol + GRAM_OFF, ad, ad, gdesc, (c | k) != 0 ? 1u : 0u);
+          }
           umma_commit(BAR(B_EMPTY + slot));
         }
         if (!ok) break;
@@ -342,35 +384,32 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;     // token row of the tile = TMEM lane
     const uint32_t owner = (uint32_t)(row / TPC);
-    uint32_t q = 0;
     int lt = 0;
     bool ok = true;
     for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
-      float ss = 0.f;
-      for (int c = 0; c < CH; ++c, ++q) {
-        const uint32_t slot = q % RING, ph = (q / RING) & 1u;
-        if (!WAIT_WARP(false, BAR(B_FULL + slot), ph)) { ok = false; break; }
-        if (c == 0 && warp == W_ROW && lane == 0) TC_TRACE(T_R_FULL0);
-        const uint8_t *rp = base + L.ring + slot * CHUNK + row * 128;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ss += sq8(*reinterpret_cast<const uint4 *>(rp + ((u ^ (row & 7)) << 4)));
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(B_EMPTY + slot));
-      }
-      if (!ok) break;
       const int buf = lt & 1;
       const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
       if (!WAIT_WARP(false, BAR(B_ACCF + buf), aph)) { ok = false; break; }
       if (warp == W_ROW && lane == 0) TC_TRACE(T_R_ACCF);
+      if (lane == 0) TC_TRACE_CH(6, quad);
       tc_fence_after();
+      const uint32_t tb = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * ACC_STRIDE;
       float d[NB];
 #pragma unroll
       for (int c16 = 0; c16 < NB / 16; ++c16) {
         float t16[16];
-        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * 64u + (uint32_t)c16 * 16u, t16);
+        tmem_ld16(tb + (uint32_t)c16 * 16u, t16);
 #pragma unroll
         for (int i = 0; i < 16; ++i) d[c16 * 16 + i] = t16[i];
+      }
+      // Gram diagonal: this lane's row is column quad*32 + lane of the block
+      float ss = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float t16[16];
+        tmem_ld16(tb + GRAM_OFF + (uint32_t)(quad * 32 + h * 16), t16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ss = (lane == h * 16 + i) ? t16[i] : ss;
       }
       tc_fence_before();
       __syncwarp();
@@ -385,6 +424,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       const int ib = lt % IN_BUFS;
       if (!WAIT_WARP(true, BAR(B_INE + ib), ((uint32_t)(lt / IN_BUFS) & 1u) ^ 1u)) { ok = false; break; }
       if (warp == W_ROW && lane == 0) TC_TRACE(T_R_INE);
+      if (lane == 0) TC_TRACE_CH(7, quad);
       const uint32_t dst = mapa(base_u32 + L.inbox + (uint32_t)(((ib * S + (int)rank) * TPC + (row % TPC)) * IBS * 4),
                                 owner);
       const uint32_t dbar = mapa(BAR(B_INF + ib), owner);
@@ -392,27 +432,31 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       for (int v = 0; v < IBS / 4; ++v)
         st_async_v4(dst + v * 16, vals[4 * v], vals[4 * v + 1], vals[4 * v + 2], vals[4 * v + 3], dbar);
       if (warp == W_ROW && lane == 0) TC_TRACE(T_R_PUSHED);
+      if (lane == 0) TC_TRACE_CH(7, 4 + quad);
     }
     if (!ok) record_error(ERR_ROW, abort_flag);
   } else if (warp == W_COEF) {
     // ---------------- coefficient warp ----------------
     int lt = 0;
-    bool ok = true;
+    bool ok = WAIT_WARP(false, BAR(B_PHI), 0u);  // gate parameters loaded
     for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
       const int ib = lt % IN_BUFS, hb = lt % HB;
       const uint32_t iph = (uint32_t)(lt / IN_BUFS) & 1u, hph = (uint32_t)(lt / HB) & 1u;
       if (lane == 0) mbar_arrive_expect_tx(BAR(B_INF + ib), INBOX_TX);  // arm: all 8 slices' rows
       if (!WAIT_WARP(true, BAR(B_INF + ib), iph)) { ok = false; break; }
       if (lane == 0) TC_TRACE(T_C_INF);
-      float acc[FD + 1];
+      float acc[IBS];
 #pragma unroll
-      for (int j = 0; j <= FD; ++j) acc[j] = 0.f;
+      for (int j = 0; j < IBS; ++j) acc[j] = 0.f;
       if (lane < TPC) {
-#pragma unroll 1
+#pragma unroll 2
         for (int s = 0; s < S; ++s) {  // fixed order over the K slices: deterministic
-          const float *src = inbox + ((ib * S + s) * TPC + lane) * IBS;
+          const float4 *src = reinterpret_cast<const float4 *>(inbox + ((ib * S + s) * TPC + lane) * IBS);
 #pragma unroll
-          for (int j = 0; j <= FD; ++j) acc[j] += src[j];
+          for (int v = 0; v < IBS / 4; ++v) {
+            const float4 q4 = src[v];
+            acc[4 * v] += q4.x; acc[4 * v + 1] += q4.y; acc[4 * v + 2] += q4.z; acc[4 * v + 3] += q4.w;
+          }
         }
       }
       __syncwarp();
@@ -482,24 +526,28 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       }
     }
     if (!ok) record_error(ERR_COEF, abort_flag);
-  } else if (warp < W_SK + NSK) {
-    // ---------------- Sinkhorn warps: H_res of the CTA's 16 tokens ----------------
-    // (idle when the layer has no H_res segment)
+  } else if (warp == W_SK) {
+    // ---------------- Sinkhorn warp: H_res of the CTA's 16 tokens ----------------
+    // Lanes 0-15 take the tokens of local tile lt, lanes 16-31 those of tile
+    // lt+1 (idle when the layer has no H_res segment).
     if constexpr (MODE == FULL) {
-      const int wsk = warp - W_SK;
+      const int half = lane >> 4;
       int lt = 0;
       bool ok = true;
-      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
-        if (lt % NSK != wsk) continue;
-        const int hb = lt % HB;
-        const uint32_t hph = (uint32_t)(lt / HB) & 1u;
-        if (!WAIT_WARP(false, BAR(B_LGF + hb), hph)) { ok = false; break; }
-        if (lane == 0) TC_TRACE(T_SK_LGF);
-        const int64_t tok = (int64_t)tile * TM + (int)rank * TPC + lane;
-        if (lane < TPC && tok < a.T) {
+      for (int tile = (int)cid; tile < ntiles && ok; tile += 2 * (int)ncl, lt += 2) {
+        const bool two = tile + (int)ncl < ntiles;
+        if (!WAIT_WARP(false, BAR(B_LGF + lt % HB), (uint32_t)(lt / HB) & 1u)) { ok = false; break; }
+        if (two && !WAIT_WARP(false, BAR(B_LGF + (lt + 1) % HB), (uint32_t)((lt + 1) / HB) & 1u)) {
+          ok = false;
+          break;
+        }
+        TC_TRACE(T_SK_LGF);
+        const int my_lt = lt + half, hb = my_lt % HB;
+        const int64_t tok = (int64_t)(tile + half * (int)ncl) * TM + (int)rank * TPC + (lane & 15);
+        if ((half == 0 || two) && tok < a.T) {
           float hm[N * N];
 #pragma unroll
-          for (int k = 0; k < N * N; ++k) hm[k] = lg[(hb * TPC + lane) * 16 + k];
+          for (int k = 0; k < N * N; ++k) hm[k] = lg[(hb * TPC + (lane & 15)) * 16 + k];
           if (a.p.apply_sinkhorn) sinkhorn_fwd<N>(hm, a.p.sk_iters, a.p.sk_eps);
           if (a.h_res) {
 #pragma unroll
@@ -507,8 +555,11 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
           }
         }
         __syncwarp();
-        if (lane == 0) TC_TRACE(T_SK_DONE);
-        if (lane == 0) mbar_arrive(BAR(B_LGE + hb));  // logits buffer free
+        TC_TRACE(T_SK_DONE);
+        if (lane == 0) {
+          mbar_arrive(BAR(B_LGE + lt % HB));  // logits buffers free
+          if (two) mbar_arrive(BAR(B_LGE + (lt + 1) % HB));
+        }
       }
       if (!ok) record_error(ERR_SK, abort_flag);
     }
@@ -519,7 +570,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     const int vpr = cz / 8;      // 16-byte vectors per row and stream
     const int c0 = (int)rank * cz;
     const int zrow = N * cz * 2; // bytes per box token (N streams x cz columns)
-    const int qitems = ZR * vpr;
+    // item (row r, vector v) walk of a box without divisions in the loop:
+    // thread starts at item ztid and steps by NZW*32 items
+    const int r_first = ztid / vpr, v_first = ztid - r_first * vpr;
+    const int r_step = (NZW * 32) / vpr, v_step = (NZW * 32) - r_step * vpr;
     uint32_t zq = 0;             // boxes consumed so far
     int lt = 0;
     bool ok = true;
@@ -536,35 +590,43 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         if (warp == W_Z && lane == 0 && qq == 0) TC_TRACE(T_Z_BOX0);
         if (warp == W_Z && lane == 0 && qq == TM / ZR - 1) TC_TRACE(T_Z_BOX3);
         const uint8_t *box = base + L.zbuf + slot * (uint32_t)a.zbox;
-        for (int it = ztid; it < qitems; it += NZW * 32) {
-          const int r = it / vpr, v = it - r * vpr;
+        const int64_t t0 = (int64_t)tile * TM + qq * ZR;  // first token of the box
+        const int rows = a.T - t0 < ZR ? (int)(a.T - t0) : ZR;
+        __nv_bfloat16 *zb = a.z + t0 * a.C + c0;
+        for (int r = r_first, v = v_first; r < rows;) {
           const int t = qq * ZR + r;
-          const int64_t tk = (int64_t)tile * TM + t;
-          if (tk >= a.T) continue;
-          float acc[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = 0.f;
           float wv[HPN];
 #pragma unroll
           for (int v4 = 0; v4 < HPN / 4; ++v4) {
             const float4 q4 = *reinterpret_cast<const float4 *>(hps + t * HPN + 4 * v4);
             wv[4 * v4] = q4.x; wv[4 * v4 + 1] = q4.y; wv[4 * v4 + 2] = q4.z; wv[4 * v4 + 3] = q4.w;
           }
+          // fp32 accumulation in packed pairs: acc[j] holds columns 2j, 2j+1
+          uint64_t acc[4];
 #pragma unroll
           for (int st = 0; st < N; ++st) {
-            const float wi = wv[st];
-            Pack<__nv_bfloat16> pk;
-            pk.raw = *reinterpret_cast<const uint4 *>(box + r * zrow + st * cz * 2 + v * 16);
+            const uint64_t w2 = f2_pack(wv[st], wv[st]);
+            const uint4 xr = *reinterpret_cast<const uint4 *>(box + r * zrow + st * cz * 2 + v * 16);
+            const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = fmaf(wi, pk.get(e), acc[e]);
+            for (int j = 0; j < 4; ++j)
+              acc[j] = st == 0 ? f2_fma(w2, bf16x2_to_f2(xw[j]), f2_pack(0.f, 0.f))
+                               : f2_fma(w2, bf16x2_to_f2(xw[j]), acc[j]);
           }
-          Pack<__nv_bfloat16> o;
+          uint32_t ow[4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o.set(e, acc[e]);
-          *reinterpret_cast<uint4 *>(a.z + tk * a.C + c0 + v * 8) = o.raw;
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            f2_unpack(acc[j], lo, hi);
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+            ow[j] = *reinterpret_cast<const uint32_t *>(&h2);
+          }
+          *reinterpret_cast<uint4 *>(zb + (int64_t)r * a.C + v * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          r += r_step;
+          v += v_step;
+          if (v >= vpr) { v -= vpr; ++r; }
         }
-        // the box may be refilled
-        fence_proxy_async_smem();
+        // the box may be refilled (read-then-overwrite: the arrive orders it)
         __syncwarp();
         if (lane == 0) mbar_arrive(BAR(B_ZE + slot));
       }
@@ -588,11 +650,13 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
 
   // ---------------- teardown ----------------
   __syncthreads();
+  TC_MARK(2);
   if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
   cluster_sync_all();  // no CTA leaves while a peer may still touch its shared memory
+  TC_MARK(3);
 #undef WAIT_WARP
 #undef BAR
 }
