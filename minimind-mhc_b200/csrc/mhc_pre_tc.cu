@@ -68,8 +68,8 @@ constexpr int W_PROD = 0, W_ZPROD = 1, W_MMA = 2, W_ROW = 3, W_COEF = 7, W_SK = 
 constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
 constexpr int HB = 4;                // weights / logits buffers (tiles in flight after the coefficients)
 // TMEM per accumulator buffer: projection (NB <= 64 columns) at +0, the Gram
-// block x . x^T of the chunk rows (128 columns) at +64; two buffers.
-constexpr int ACC_STRIDE = 256, GRAM_OFF = 64, TMEM_COLS = 512;
+// block x . x^T of the chunk rows (128 columns) after it; two buffers.
+constexpr int ACC_STRIDE = 256, TMEM_COLS = 512;
 
 // Per-tile timeline instrumentation (clock64 of cluster 0, CTA 0), compiled in
 // only with -DMHC_TC_TRACE; events are indexed [local tile][event].
@@ -85,7 +85,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-#define TC_MARK(i) do { if (threadIdx.x == 0) { if ((i) == 0) atomicMin(&g_trace_ns[0], gtimer()); else atomicMax(&g_trace_ns[i], gtimer()); } } while (0)
+__device__ unsigned long long g_trace_cta[256][2];  // per CTA: loop start, loop end
+#define TC_MARK(i) do { if (threadIdx.x == 0) { const unsigned long long now_ = gtimer(); \
+  if ((i) == 0) atomicMin(&g_trace_ns[0], now_); else atomicMax(&g_trace_ns[i], now_); \
+  if ((i) == 1 || (i) == 2) g_trace_cta[blockIdx.x & 255][(i) - 1] = now_; } } while (0)
 #else
 #define TC_MARK(i) do { } while (0)
 #define TC_TRACE(ev) do { } while (0)
@@ -118,12 +121,21 @@ constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ZF = 2 * RING_MAX, B_ZE = B_ZF +
 // producers and the MMA issuer, which start streaming x at once)
 constexpr int W_CONV = W_MMA + 1, NCONV = NWARPS - W_CONV;
 
+// Two operand layouts.  Merged: ring slot s is [phi chunk (s mod CH) | x
+// chunk], so one MMA with B = the whole slot (NB + 128 rows) yields the
+// projection and the Gram block while reading the x chunk once; the ring
+// length is then a multiple of CH.  Separate: plain x slots, phi in a region
+// of its own, two MMAs per K step.
+__host__ __device__ inline uint32_t slot_bytes(int merged, int NB) {
+  return (uint32_t)CHUNK + (merged ? (uint32_t)NB * 128 : 0u);
+}
+
 __host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR, int RING, int ZS,
-                                              int zbox) {
+                                              int zbox, int merged) {
   Layout L;
   uint32_t o = 0;
-  L.ring = o;  o += (uint32_t)RING * CHUNK;
-  L.phi = o;   o += (uint32_t)CH * NB * 128;
+  L.ring = o;  o += (uint32_t)RING * slot_bytes(merged, NB);
+  L.phi = o;   o += merged ? 0u : (uint32_t)CH * NB * 128;
   L.zbuf = o;  o += (uint32_t)ZS * zbox;
   L.inbox = o; o += (uint32_t)IN_BUFS * S * TPC * IBS * 4;
   L.hp = o;    o += (uint32_t)HB * TM * HPN * 4;
@@ -140,6 +152,7 @@ struct Args {
   int64_t T;
   int C, nC, KS, CH;
   int RING, ZS, zbox;   // x ring slots, pre-aggregate box slots, box bytes
+  int merged;           // operand layout (see make_layout)
   const void *phi;
   CoefParams p;
   __nv_bfloat16 *z;
@@ -148,11 +161,10 @@ struct Args {
   float *inv_rms, *mixes;
 };
 
-// byte offset of element (row j, k) of the phi slice: chunk-major, 128-byte
-// swizzled K-major rows (granule index XOR row-in-atom)
-__device__ __forceinline__ uint32_t phi_off(int j, int k, int NB) {
-  const int c = k >> 6, kk = k & 63;
-  return (uint32_t)c * NB * 128 + (j >> 3) * 1024 + (j & 7) * 128 + ((((kk >> 3) ^ (j & 7))) << 4) + ((kk & 7) << 1);
+// byte offset of element (row j, column kk < 64) inside one phi chunk block:
+// 128-byte swizzled K-major rows (granule index XOR row-in-atom)
+__device__ __forceinline__ uint32_t phi_off(int j, int kk, int NB) {
+  return (uint32_t)(j >> 3) * 1024 + (j & 7) * 128 + ((((kk >> 3) ^ (j & 7))) << 4) + ((kk & 7) << 1);
 }
 
 __device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
@@ -186,8 +198,11 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t *base = smem_raw + (base_u32 - raw_u32);
-  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR, a.RING, a.ZS, a.zbox);
+  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR, a.RING, a.ZS, a.zbox, a.merged);
   const int RING = a.RING, ZS = a.ZS;
+  const uint32_t SLOT = slot_bytes(a.merged, NB);
+  const uint32_t XOFF = a.merged ? (uint32_t)NB * 128u : 0u;  // x chunk offset inside a slot
+  const uint32_t GRAM = a.merged ? (uint32_t)NB : 64u;         // Gram block column in the accumulator
   float *inbox = reinterpret_cast<float *>(base + L.inbox);
   float *hp = reinterpret_cast<float *>(base + L.hp);
   float *lg = reinterpret_cast<float *>(base + L.lg);
@@ -251,7 +266,14 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     // deep so their latencies overlap.
     const int ctid = tid - W_CONV * 32, nconv = NCONV * 32;
     const int k0 = (int)rank * a.KS, total = a.KS * FD;
-    uint8_t *phs = base + L.phi;
+    // destination of K column k (chunk k / 64): the chunk's phi block (merged:
+    // one copy in front of every ring slot holding that chunk index)
+    const int copies = a.merged ? RING / a.CH : 1;
+    auto phi_dst = [&](int cp, int j, int k) -> uint8_t * {
+      const int c = k >> 6;
+      uint8_t *blk = a.merged ? base + L.ring + (uint32_t)(cp * a.CH + c) * SLOT : base + L.phi + (uint32_t)c * NB * 128;
+      return blk + phi_off(j, k & 63, NB);
+    };
     for (int e0 = ctid; e0 < total; e0 += 8 * nconv) {
       float v[8];
 #pragma unroll
@@ -269,8 +291,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
           const int k = e / FD, j = e - k * FD;
           const __nv_bfloat16 hi = __float2bfloat16_rn(v[u]);
           const __nv_bfloat16 lo = __float2bfloat16_rn(v[u] - __bfloat162float(hi));
-          *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = hi;
-          *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j + FD, k, NB)) = lo;
+          for (int cp = 0; cp < copies; ++cp) {
+            *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j, k)) = hi;
+            *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j + FD, k)) = lo;
+          }
         }
       }
     }
@@ -278,7 +302,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     if constexpr (PADR > 0) {
       for (int e = ctid; e < a.KS * PADR; e += nconv) {
         const int k = e / PADR, j = 2 * FD + (e - (e / PADR) * PADR);
-        *reinterpret_cast<__nv_bfloat16 *>(phs + phi_off(j, k, NB)) = __float2bfloat16_rn(0.f);
+        for (int cp = 0; cp < copies; ++cp)
+          *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j, k)) = __float2bfloat16_rn(0.f);
       }
     }
     load_params_tc<N, MODE>(par, a.p, ctid, nconv);
@@ -302,7 +327,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
           if (c == 0) TC_TRACE(T_P_FIRST);
           if (c == CH - 1) TC_TRACE(T_P_LAST);
           mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
-          tma_load_2d(base_u32 + L.ring + slot * CHUNK, &tmap, (int)rank * a.KS + c * 64, tile * TM,
+          tma_load_2d(base_u32 + L.ring + slot * SLOT + XOFF, &tmap, (int)rank * a.KS + c * 64, tile * TM,
                       BAR(B_FULL + slot));
         }
       }
@@ -342,6 +367,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_f32(128, NB);
       constexpr uint32_t gdesc = umma_idesc_bf16_f32(128, 128);
+      constexpr uint32_t mdesc = umma_idesc_bf16_f32(128, NB + 128);
       uint32_t q = 0;
       int lt = 0;
       bool ok = wait_parity<false>(BAR(B_PHI), 0u, abort_flag);  // phi slice converted
@@ -357,15 +383,22 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
           if (!wait_parity<false>(BAR(B_FULL + slot), ph, abort_flag)) { ok = false; break; }
           TC_TRACE_CH(c, 1);
           tc_fence_after();
-          const uint32_t a0 = base_u32 + L.ring + slot * CHUNK;
-          const uint32_t b0 = base_u32 + L.phi + (uint32_t)c * NB * 128u;
+          // sum of squares of each row = diagonal of x . x^T: the chunk is
+          // (part of) its own B operand (same K-major 128-byte-swizzled rows)
+          const uint32_t s0 = base_u32 + L.ring + slot * SLOT;
+          const uint32_t a0 = s0 + XOFF;
+          if (a.merged) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = umma_desc_sw128(a0 + k * 32);
-            umma_bf16(dcol, ad, umma_desc_sw128(b0 + k * 32), idesc, (c | k) != 0 ? 1u : 0u);
-            // sum of squares of each row = diagonal of x . x^T: the chunk is
-            // its own B operand (same K-major 128 x 64 layout)
-            umma_bf16(dcol + GRAM_OFF, ad, ad, gdesc, (c | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k)
+              umma_bf16(dcol, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(s0 + k * 32), mdesc, (c | k) != 0 ? 1u : 0u);
+          } else {
+            const uint32_t b0 = base_u32 + L.phi + (uint32_t)c * NB * 128u;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = umma_desc_sw128(a0 + k * 32);
+              umma_bf16(dcol, ad, umma_desc_sw128(b0 + k * 32), idesc, (c | k) != 0 ? 1u : 0u);
+              umma_bf16(dcol + GRAM, ad, ad, gdesc, (c | k) != 0 ? 1u : 0u);
+            }
           }
           umma_commit(BAR(B_EMPTY + slot));
         }
@@ -407,7 +440,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float t16[16];
-        tmem_ld16(tb + GRAM_OFF + (uint32_t)(quad * 32 + h * 16), t16);
+        tmem_ld16(tb + GRAM + (uint32_t)(quad * 32 + h * 16), t16);
 #pragma unroll
         for (int i = 0; i < 16; ++i) ss = (lane == h * 16 + i) ? t16[i] : ss;
       }
@@ -680,25 +713,40 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block on sm_100
 
-// Ring / box slot counts that fit the shared-memory budget.
+// Operand layout and ring / box slot counts that fit the shared-memory budget:
+// the merged layout with the longest ring (4..8 slots, a multiple of CH) and at
+// least two pre-aggregate boxes in flight, else the separate layout.
 template <int N, int MODE>
-static bool pick_slots(int CH, int zbox, int &ring, int &zs) {
+static bool pick_slots(int CH, int zbox, int &ring, int &zs, int &merged) {
   using Cf = Cfg<N, MODE>;
-  // (x chunks, quarter-tile boxes) in flight, in order of preference
-#if defined(MHC_TC_RING) && defined(MHC_TC_ZS)
-  const int prefs[][2] = {{MHC_TC_RING, MHC_TC_ZS}};
+  auto fits = [&](int r, int z, int m) {
+    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, r, z, zbox, m);
+    return (size_t)L.total + 1024 <= SMEM_LIMIT;
+  };
+#if defined(MHC_TC_RING) && defined(MHC_TC_ZS) && defined(MHC_TC_MERGED)
+  ring = MHC_TC_RING;
+  zs = MHC_TC_ZS;
+  merged = MHC_TC_MERGED;
+  return fits(ring, zs, merged) && (!merged || ring % CH == 0);
 #else
+  for (int r = (RING_MAX / CH) * CH; r >= 4; r -= CH)
+    for (int z : {3, 2})
+      if (fits(r, z, 1)) {
+        ring = r;
+        zs = z;
+        merged = 1;
+        return true;
+      }
   const int prefs[][2] = {{5, 3}, {4, 4}, {6, 2}, {4, 3}, {4, 2}, {3, 2}};
-#endif
-  for (const auto &pr : prefs) {
-    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, pr[0], pr[1], zbox);
-    if ((size_t)L.total + 1024 <= SMEM_LIMIT) {
+  for (const auto &pr : prefs)
+    if (fits(pr[0], pr[1], 0)) {
       ring = pr[0];
       zs = pr[1];
+      merged = 0;
       return true;
     }
-  }
   return false;
+#endif
 }
 
 template <int N, int MODE>
@@ -706,8 +754,9 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
   using Cf = Cfg<N, MODE>;
   const int nC = N * C;
   args.zbox = ZR * N * (C / S) * 2;
-  if (!pick_slots<N, MODE>(args.CH, args.zbox, args.RING, args.ZS)) return cudaErrorNotSupported;
-  const Layout L = make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox);
+  if (!pick_slots<N, MODE>(args.CH, args.zbox, args.RING, args.ZS, args.merged)) return cudaErrorNotSupported;
+  const Layout L =
+      make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox, args.merged);
   const size_t smem = (size_t)L.total + 1024;
   auto kern = pre_tc_kernel<N, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -801,6 +850,7 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
   a.RING = 0;
   a.ZS = 0;
   a.zbox = 0;
+  a.merged = 0;
   a.phi = phi;
   a.p = p;
   a.z = reinterpret_cast<__nv_bfloat16 *>(z);
