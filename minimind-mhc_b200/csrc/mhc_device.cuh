@@ -128,6 +128,14 @@ __device__ __forceinline__ void store_vec_stream(T *p, const float (&v)[V]) {
   }
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the previous kernel of the stream is still
+// running; it must call grid_dep_wait() before reading anything an earlier
+// kernel wrote (the wait returns at once when there is no such kernel).
+// grid_dep_launch() lets the next kernel of the stream start early.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Hardware reciprocal (rcp.approx.ftz.f32, within 1 ulp for normal inputs).
 // The reference's Triton kernels divide with Triton's default fp32 division,
 // which is approximate as well (model/mhc_fused.py:86-91, 210, 252-253); the

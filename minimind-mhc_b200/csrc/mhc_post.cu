@@ -59,6 +59,8 @@ post_fwd_kernel(const Tx *__restrict__ x, const void *__restrict__ h_res, int hr
   constexpr int VEC = 16 / sizeof(Tx);
   constexpr int NCOEF = (HAS_RES ? N * N : 0) + N;
   extern __shared__ float cs[];  // [TB][NCOEF]
+  grid_dep_launch();
+  grid_dep_wait();
   const int64_t tok0 = (int64_t)blockIdx.x * TB;
   const int tb = stage_post_coefs<N, HAS_RES, SK>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB, sk_iters,
                                                   sk_eps, h_res_out);
@@ -106,6 +108,8 @@ post_fwd_scalar_kernel(const void *__restrict__ x, int x_dt, const void *__restr
                        void *__restrict__ h_res_out) {
   constexpr int NCOEF = (HAS_RES ? N * N : 0) + N;
   extern __shared__ float cs[];
+  grid_dep_launch();
+  grid_dep_wait();
   const int64_t tok0 = (int64_t)blockIdx.x * TB;
   const int tb = stage_post_coefs<N, HAS_RES, SK>(cs, h_res, hr_dt, h_post, hp_dt, T, tok0, TB, sk_iters,
                                                   sk_eps, h_res_out);
@@ -323,7 +327,20 @@ cudaError_t launch_post_fwd(int n, int x_dtype, const void *x, const void *h_res
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
       }
-      kern<<<grid, 256, smem, stream>>>(args...);
+      // programmatic dependent launch: the kernel waits (griddepcontrol) for
+      // the previous kernel of the stream before its first global read
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cfg.gridDim = dim3(grid, 1, 1);
+      cfg.blockDim = dim3(256, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+      if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
     if (!vecok) {

@@ -41,6 +41,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "mhc_device.cuh"
 #include "mhc_dispatch.cuh"
 #include "mhc_kernels.h"
@@ -58,7 +60,8 @@ constexpr int S = 8;                 // CTAs per cluster (K split)
 constexpr int TM = 128;              // tokens per tile (UMMA M)
 constexpr int RING_MAX = 8;          // x chunk slots (runtime count <= this)
 constexpr int ZS_MAX = 8;            // pre-aggregate box slots (runtime count <= this)
-constexpr int ZR = 32;               // tokens per pre-aggregate box (a quarter tile)
+// tokens per pre-aggregate box: 32 or 16 (a quarter or an eighth of a tile),
+// chosen with the number of boxes in flight to fit shared memory
 constexpr int CHUNK = TM * 128;      // 128 rows x 128 bytes
 constexpr int TPC = TM / S;          // tokens whose coefficients a CTA finalises
 constexpr int NWARPS = 17, NTHREADS = NWARPS * 32;
@@ -153,6 +156,7 @@ struct Args {
   int C, nC, KS, CH;
   int RING, ZS, zbox;   // x ring slots, pre-aggregate box slots, box bytes
   int merged;           // operand layout (see make_layout)
+  int ZR;               // tokens per pre-aggregate box
   const void *phi;
   CoefParams p;
   __nv_bfloat16 *z;
@@ -260,6 +264,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   __syncthreads();
   cluster_sync_all();        // every CTA's barriers exist before any remote arrive or st.async
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
+  // set-up above overlaps the previous kernel of the stream (programmatic
+  // dependent launch); every input read comes after this wait
+  grid_dep_launch();
+  grid_dep_wait();
   if (warp >= W_CONV) {
     // phi slice of this CTA -> bf16 hi | lo, K-major, 128-byte swizzle, while
     // the producer already streams the first x chunks.  Loads are batched 8
@@ -274,7 +282,39 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       uint8_t *blk = a.merged ? base + L.ring + (uint32_t)(cp * a.CH + c) * SLOT : base + L.phi + (uint32_t)c * NB * 128;
       return blk + phi_off(j, k & 63, NB);
     };
-    for (int e0 = ctid; e0 < total; e0 += 8 * nconv) {
+    auto put = [&](int k, int j, float v) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+      for (int cp = 0; cp < copies; ++cp) {
+        *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j, k)) = hi;
+        *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j + FD, k)) = lo;
+      }
+    };
+    constexpr int FQ = FD % 4 == 0 ? FD / 4 : 1;  // 16-byte quads per phi row
+    const bool vec = (FD % 4 == 0) && a.p.param_dtype == MHC_F32 && ((uintptr_t)a.phi & 15) == 0;
+    if (vec) {
+      // fp32 phi rows are FD contiguous floats: 16-byte loads, 8 in flight
+      const float4 *src = reinterpret_cast<const float4 *>(a.phi) + (int64_t)k0 * FQ;
+      const int quads = a.KS * FQ;
+      for (int e0 = ctid; e0 < quads; e0 += 8 * nconv) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (e0 + u * nconv < quads) v[u] = src[e0 + u * nconv];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int e = e0 + u * nconv;
+          if (e < quads) {
+            const int k = e / FQ, j = (e - k * FQ) * 4;
+            put(k, j, v[u].x);
+            put(k, j + 1, v[u].y);
+            put(k, j + 2, v[u].z);
+            put(k, j + 3, v[u].w);
+          }
+        }
+      }
+    }
+    for (int e0 = ctid; !vec && e0 < total; e0 += 8 * nconv) {
       float v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -289,12 +329,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         const int e = e0 + u * nconv;
         if (e < total) {
           const int k = e / FD, j = e - k * FD;
-          const __nv_bfloat16 hi = __float2bfloat16_rn(v[u]);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(v[u] - __bfloat162float(hi));
-          for (int cp = 0; cp < copies; ++cp) {
-            *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j, k)) = hi;
-            *reinterpret_cast<__nv_bfloat16 *>(phi_dst(cp, j + FD, k)) = lo;
-          }
+          put(k, j, v[u]);
         }
       }
     }
@@ -349,11 +384,11 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         const uint32_t hph = (uint32_t)(lt / HB) & 1u;
         if (!wait_parity<false>(BAR(B_ZGO + hb), hph, abort_flag)) { ok = false; break; }
         TC_TRACE(T_ZP_GO);
-        for (int qq = 0; qq < TM / ZR; ++qq, ++zq) {
+        for (int qq = 0; qq < TM / a.ZR; ++qq, ++zq) {
           const uint32_t slot = zq % ZS, zph = (zq / ZS) & 1u;
           if (!wait_parity<false>(BAR(B_ZE + slot), zph ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(BAR(B_ZF + slot), (uint32_t)a.zbox);
-          tma_load_3d(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0, tile * TM + qq * ZR,
+          tma_load_3d(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0, tile * TM + qq * a.ZR,
                       BAR(B_ZF + slot));
         }
       }
@@ -599,6 +634,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   } else {
     // ---------------- pre-aggregate warps ----------------
     const int ztid = tid - W_Z * 32;
+    const int ZR = a.ZR;
     const int cz = a.C / S;      // columns of z owned by this CTA
     const int vpr = cz / 8;      // 16-byte vectors per row and stream
     const int c0 = (int)rank * cz;
@@ -717,55 +753,65 @@ constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block
 // the merged layout with the longest ring (4..8 slots, a multiple of CH) and at
 // least two pre-aggregate boxes in flight, else the separate layout.
 template <int N, int MODE>
-static bool pick_slots(int CH, int zbox, int &ring, int &zs, int &merged) {
+static bool pick_slots(int CH, int C, Args &a) {
   using Cf = Cfg<N, MODE>;
-  auto fits = [&](int r, int z, int m) {
-    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, r, z, zbox, m);
+  auto fits = [&](int r, int z, int zr, int m) {
+    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, r, z, zr * N * (C / S) * 2, m);
     return (size_t)L.total + 1024 <= SMEM_LIMIT;
   };
-#if defined(MHC_TC_RING) && defined(MHC_TC_ZS) && defined(MHC_TC_MERGED)
-  ring = MHC_TC_RING;
-  zs = MHC_TC_ZS;
-  merged = MHC_TC_MERGED;
-  return fits(ring, zs, merged) && (!merged || ring % CH == 0);
+  auto take = [&](int r, int z, int zr, int m) {
+    a.RING = r;
+    a.ZS = z;
+    a.ZR = zr;
+    a.zbox = zr * N * (C / S) * 2;
+    a.merged = m;
+    return true;
+  };
+#if defined(MHC_TC_RING) && defined(MHC_TC_ZS) && defined(MHC_TC_MERGED) && defined(MHC_TC_ZR)
+  return fits(MHC_TC_RING, MHC_TC_ZS, MHC_TC_ZR, MHC_TC_MERGED) && (!MHC_TC_MERGED || MHC_TC_RING % CH == 0) &&
+         take(MHC_TC_RING, MHC_TC_ZS, MHC_TC_ZR, MHC_TC_MERGED);
 #else
+  // pre-aggregate (tokens per box, boxes in flight): quarter-tile boxes first
+  const int zopts[][2] = {{32, 3}, {32, 2}, {16, 4}, {16, 3}};
   for (int r = (RING_MAX / CH) * CH; r >= 4; r -= CH)
-    for (int z : {3, 2})
-      if (fits(r, z, 1)) {
-        ring = r;
-        zs = z;
-        merged = 1;
-        return true;
-      }
+    for (const auto &zo : zopts)
+      if (fits(r, zo[1], zo[0], 1)) return take(r, zo[1], zo[0], 1);
   const int prefs[][2] = {{5, 3}, {4, 4}, {6, 2}, {4, 3}, {4, 2}, {3, 2}};
   for (const auto &pr : prefs)
-    if (fits(pr[0], pr[1], 0)) {
-      ring = pr[0];
-      zs = pr[1];
-      merged = 0;
-      return true;
-    }
+    for (int zr : {32, 16})
+      if (fits(pr[0], pr[1], zr, 0)) return take(pr[0], pr[1], zr, 0);
   return false;
 #endif
 }
 
-template <int N, int MODE>
-static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaStream_t stream) {
-  using Cf = Cfg<N, MODE>;
-  const int nC = N * C;
-  args.zbox = ZR * N * (C / S) * 2;
-  if (!pick_slots<N, MODE>(args.CH, args.zbox, args.RING, args.ZS, args.merged)) return cudaErrorNotSupported;
-  const Layout L =
-      make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox, args.merged);
-  const size_t smem = (size_t)L.total + 1024;
-  auto kern = pre_tc_kernel<N, MODE>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+// Host-side per-call work is cached: the tensor maps of the last few x
+// tensors (keyed by address and shape; a map holds nothing else), and per
+// kernel instantiation the dynamic shared memory size already granted and the
+// co-resident cluster count for a given size.
+struct MapEntry {
+  const void *x;
+  int64_t T;
+  int C, N, ZR, dev;
+  CUtensorMap tmap, zmap;
+};
+struct KernEntry {
+  const void *kern;
+  int dev;
+  size_t smem_set;   // largest dynamic shared memory size requested so far
+  size_t smem_occ;   // size the cluster count below was computed for
+  int clusters;
+};
+static std::mutex g_host_mu;
+static MapEntry g_maps[8];
+static int g_maps_n = 0, g_maps_next = 0;
+static KernEntry g_kerns[64];
+static int g_kerns_n = 0;
 
+static bool encode_maps(const void *x, int64_t T, int C, int N, int ZR, CUtensorMap &tmap, CUtensorMap &zmap) {
   auto enc = encode_fn();
-  if (!enc) return cudaErrorNotSupported;
+  if (!enc) return false;
+  const int nC = N * C;
   // x as (T rows) x (nC columns): 128-row x 64-column K chunks, 128-byte swizzle
-  CUtensorMap tmap;
   {
     const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
     const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
@@ -774,10 +820,9 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
     if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorNotSupported;
+      return false;
   }
   // x as (T) x (n streams) x (C columns): boxes of ZR tokens x n streams x C/8 columns
-  CUtensorMap zmap;
   {
     const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)N, (cuuint64_t)T};
     const cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)nC * 2};
@@ -786,36 +831,91 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
     if (enc(&zmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(x), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorNotSupported;
+      return false;
   }
+  return true;
+}
+
+template <int N, int MODE>
+static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaStream_t stream) {
+  using Cf = Cfg<N, MODE>;
+  if (!pick_slots<N, MODE>(args.CH, C, args)) return cudaErrorNotSupported;
+  const Layout L =
+      make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox, args.merged);
+  const size_t smem = (size_t)L.total + 1024;
+  auto kern = pre_tc_kernel<N, MODE>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
 
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // cluster shape only for the occupancy query
   cfg.blockDim = dim3(NTHREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  static int max_clusters[64][3][5];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int ni = N == 1 ? 0 : N == 2 ? 1 : N == 4 ? 2 : N == 8 ? 3 : 4;
-  int &mc = max_clusters[dev & 63][MODE][ni];
-  if (mc == 0) {
-    cfg.gridDim = dim3(S * 64, 1, 1);
-    int v = 0;
-    e = cudaOccupancyMaxActiveClusters(&v, (void *)kern, &cfg);
-    if (e != cudaSuccess) return e;
-    if (v <= 0) return cudaErrorNotSupported;
-    mc = v;
+
+  CUtensorMap tmap, zmap;
+  int max_clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_host_mu);
+    KernEntry *ke = nullptr;
+    for (int i = 0; i < g_kerns_n; ++i)
+      if (g_kerns[i].kern == (const void *)kern && g_kerns[i].dev == dev) ke = &g_kerns[i];
+    if (!ke) {
+      if (g_kerns_n == 64) return cudaErrorNotSupported;
+      ke = &g_kerns[g_kerns_n++];
+      *ke = KernEntry{(const void *)kern, dev, 0, 0, 0};
+    }
+    if (smem > ke->smem_set) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      ke->smem_set = smem;
+    }
+    if (ke->smem_occ != smem || ke->clusters <= 0) {
+      cfg.gridDim = dim3(S * 64, 1, 1);
+      int v = 0;
+      e = cudaOccupancyMaxActiveClusters(&v, (void *)kern, &cfg);
+      if (e != cudaSuccess) return e;
+      if (v <= 0) return cudaErrorNotSupported;
+      ke->smem_occ = smem;
+      ke->clusters = v;
+    }
+    max_clusters = ke->clusters;
+
+    int hit = -1;
+    for (int i = 0; i < g_maps_n; ++i)
+      if (g_maps[i].x == x && g_maps[i].T == T && g_maps[i].C == C && g_maps[i].N == N && g_maps[i].ZR == args.ZR &&
+          g_maps[i].dev == dev)
+        hit = i;
+    if (hit < 0) {
+      MapEntry &m = g_maps[g_maps_next];
+      if (!encode_maps(x, T, C, N, args.ZR, m.tmap, m.zmap)) return cudaErrorNotSupported;
+      m.x = x;
+      m.T = T;
+      m.C = C;
+      m.N = N;
+      m.ZR = args.ZR;
+      m.dev = dev;
+      hit = g_maps_next;
+      g_maps_next = (g_maps_next + 1) % 8;
+      if (g_maps_n < 8) ++g_maps_n;
+    }
+    tmap = g_maps[hit].tmap;
+    zmap = g_maps[hit].zmap;
   }
+
   const int64_t ntiles = (T + TM - 1) / TM;
-  const int clusters = (int)(ntiles < mc ? ntiles : mc);
+  const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
   cfg.gridDim = dim3((unsigned)(clusters * S), 1, 1);
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, tmap, zmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
@@ -851,6 +951,7 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
   a.ZS = 0;
   a.zbox = 0;
   a.merged = 0;
+  a.ZR = 32;
   a.phi = phi;
   a.p = p;
   a.z = reinterpret_cast<__nv_bfloat16 *>(z);
