@@ -1,0 +1,115 @@
+"""Token sharding across ranks, checked on CPU with gloo (world size 2).
+
+The mHC path shards by token: each rank runs its own tokens with no collective
+in the forward pass, and only the parameter gradients are summed across ranks
+(DDP / NCCL in training).  These tests run two gloo ranks as child processes
+and check, with the oracle, that
+
+* the sharded forward equals the single-process forward on the concatenated
+  tokens, row for row;
+* all-reduced (summed) parameter gradients equal the full-batch gradients;
+* the timing reduction used by ``bench.py`` (max over ranks) picks the slowest
+  rank.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import mhc_oracle as O
+
+N, C, T_PER_RANK, WORLD = 4, 64, 24, 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _params():
+    gen = torch.Generator().manual_seed(0)
+    return O.make_full_params(N, C, init="bench", generator=gen)
+
+
+def _inputs(rank):
+    gen = torch.Generator().manual_seed(100 + rank)
+    return torch.randn(1, T_PER_RANK, N * C, generator=gen)
+
+
+def _loss(p, x):
+    out = O.full_forward(x, p, lambda z: z * 0.5, N, C, sinkhorn_iters=20)
+    return out, (out.float() ** 2).mean() * out.numel()
+
+
+def _worker(rank, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        p = _params()
+        leaves = [p.phi_weight, p.alpha_pre, p.bias_pre, p.alpha_post, p.bias_post, p.alpha_res, p.bias_res]
+        for t in leaves:
+            t.requires_grad_(True)
+        out, loss = _loss(p, _inputs(rank))
+        loss.backward()
+        gs = [t.grad.clone() for t in leaves]
+        for g in gs:
+            dist.all_reduce(g, op=dist.ReduceOp.SUM)
+        # bench.py reduces the step time with a max over ranks
+        t = torch.tensor([1.0 + rank])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        # numpy copies pickle by value (tensors would be shared through file
+        # descriptors that vanish when this process exits)
+        q.put((rank, out.detach().numpy().copy(), [g.numpy().copy() for g in gs], t.item()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def sharded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    for pr in procs:
+        pr.start()
+    res = {}
+    for _ in range(WORLD):
+        r, out, gs, tmax = q.get(timeout=300)
+        res[r] = (torch.from_numpy(out), [torch.from_numpy(g) for g in gs], tmax)
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    return res
+
+
+def test_sharded_forward_matches_single_process(sharded):
+    p = _params()
+    x = torch.cat([_inputs(r) for r in range(WORLD)], dim=1)
+    with torch.no_grad():
+        full, _ = _loss(p, x)
+    for r in range(WORLD):
+        shard = full[:, r * T_PER_RANK:(r + 1) * T_PER_RANK]
+        assert torch.allclose(sharded[r][0], shard, rtol=1e-6, atol=1e-6)
+
+
+def test_allreduced_grads_equal_full_batch_grads(sharded):
+    p = _params()
+    leaves = [p.phi_weight, p.alpha_pre, p.bias_pre, p.alpha_post, p.bias_post, p.alpha_res, p.bias_res]
+    for t in leaves:
+        t.requires_grad_(True)
+    x = torch.cat([_inputs(r) for r in range(WORLD)], dim=1)
+    _, loss = _loss(p, x)
+    loss.backward()
+    for r in range(WORLD):
+        for g_shard, t in zip(sharded[r][1], leaves):
+            assert torch.allclose(g_shard, t.grad, rtol=1e-4, atol=1e-5)
+
+
+def test_step_time_is_max_over_ranks(sharded):
+    assert all(sharded[r][2] == float(WORLD) for r in range(WORLD))
