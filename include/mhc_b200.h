@@ -269,6 +269,28 @@ int mhc_last_path(void);
  */
 int mhc_device_error(int clear);
 
+/*
+ * mhc_pre_fwd without a caller workspace: the same arguments and results as
+ * mhc_pre_fwd minus (workspace, workspace_bytes).  Scratch is a fixed 16 MiB
+ * device array inside the library (a file-scope __device__ variable; its
+ * address is looked up once per device, on the first call on that device --
+ * make that first call outside any stream capture).  Limit: T*n <= 4,194,304;
+ * larger batches are rejected with MHC_ERR_WORKSPACE before any CUDA call.
+ * Nothing is allocated and nothing in the scratch needs to start at zero.
+ * All calls on one device share the scratch: two calls that overlap in time
+ * (different streams or threads) race on it.
+ * No counterpart in the reference (its launches allocate through the PyTorch
+ * caching allocator, model/mhc_fused.py:589-595).
+ */
+int mhc_pre_fwd_noalloc(const void *x, int x_dtype, int64_t T, int n, int C,
+                        const void *phi, const void *alpha_pre, const void *bias_pre,
+                        const void *alpha_post, const void *bias_post,
+                        const void *alpha_res, const void *bias_res, int param_dtype,
+                        int with_res, int apply_sinkhorn, int sinkhorn_iters,
+                        float post_mult, float pre_eps, float rms_eps, float sinkhorn_eps,
+                        void *z, void *h_pre, void *h_post, void *h_res, int coef_dtype,
+                        float *inv_rms, float *mixes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

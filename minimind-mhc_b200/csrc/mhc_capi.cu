@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "mhc_b200.h"
 #include "mhc_dispatch.cuh"
@@ -368,6 +369,66 @@ int mhc_stream_expand_bwd(const void *dout, void *dx, int dtype, int64_t T, int 
   if (!dout || !dx) return fail(MHC_ERR_NULL, "mhc_stream_expand_bwd: NULL pointer");
   return cuda_status(launch_expand_bwd(dtype, dout, dx, T, n, C, reinterpret_cast<cudaStream_t>(stream)),
                      "mhc_stream_expand_bwd");
+}
+
+/* ------------------------------------------------------------------------ */
+/* mhc_pre_fwd without a caller workspace                                    */
+/* ------------------------------------------------------------------------ */
+
+}  // extern "C"
+
+namespace mhc {
+// Fixed device scratch of mhc_pre_fwd_noalloc: 16 MiB, enough for T*n <=
+// 4,194,304 (the generic path's per-token fp32 gate weights).  Every word the
+// kernels read from it is written earlier in the same call, so nothing in it
+// has to start at zero.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_ptr[128] = {nullptr};
+
+// Device address of the scratch on the current device, looked up once per
+// device (the first call on a device does the lookup).
+static int noalloc_scratch(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "mhc_pre_fwd_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 128) return fail(MHC_ERR_UNSUPPORTED, "mhc_pre_fwd_noalloc: device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "mhc_pre_fwd_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MHC_OK;
+}
+}  // namespace mhc
+
+extern "C" {
+
+int mhc_pre_fwd_noalloc(const void *x, int x_dtype, int64_t T, int n, int C, const void *phi,
+                        const void *alpha_pre, const void *bias_pre, const void *alpha_post,
+                        const void *bias_post, const void *alpha_res, const void *bias_res,
+                        int param_dtype, int with_res, int apply_sinkhorn, int sinkhorn_iters,
+                        float post_mult, float pre_eps, float rms_eps, float sinkhorn_eps, void *z,
+                        void *h_pre, void *h_post, void *h_res, int coef_dtype, float *inv_rms,
+                        float *mixes, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  const size_t need = mhc_pre_fwd_workspace(T, n, C, with_res);
+  if (need > kNoAllocScratchBytes)
+    return fail(MHC_ERR_WORKSPACE,
+                "mhc_pre_fwd_noalloc: T=%lld x n=%d needs %zu bytes of scratch; the fixed device scratch "
+                "holds %zu (T*n <= %zu); use mhc_pre_fwd with a workspace",
+                (long long)T, n, need, kNoAllocScratchBytes, kNoAllocScratchBytes / 4);
+  void *scratch = nullptr;
+  if (T > 0) MHC_TRY(noalloc_scratch(&scratch));
+  return mhc_pre_fwd(x, x_dtype, T, n, C, phi, alpha_pre, bias_pre, alpha_post, bias_post, alpha_res,
+                     bias_res, param_dtype, with_res, apply_sinkhorn, sinkhorn_iters, post_mult, pre_eps,
+                     rms_eps, sinkhorn_eps, z, h_pre, h_post, h_res, coef_dtype, inv_rms, mixes, scratch,
+                     scratch ? kNoAllocScratchBytes : 0, stream);
 }
 
 }  // extern "C"
