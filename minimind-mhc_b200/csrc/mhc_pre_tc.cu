@@ -29,7 +29,7 @@
 //               CTAs with st.async and writes the per-token outputs.
 //   warp 8      Sinkhorn warp: H_res of the CTA's 16 tokens of two tiles at
 //               a time (one token per lane, matrix in registers).  The logits
-//               are 4-deep buffered, so the 20 iterations stay off the tile's
+//               are 3-deep buffered, so the 20 iterations stay off the tile's
 //               critical path.
 //   warps 9-16  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] from the
 //               staged boxes, fp32 accumulation in packed pairs.
@@ -69,7 +69,17 @@ constexpr int NWARPS = 17, NTHREADS = NWARPS * 32;
 // mbarrier holds up every other branch of its warp.
 constexpr int W_PROD = 0, W_ZPROD = 1, W_MMA = 2, W_ROW = 3, W_COEF = 7, W_SK = 8, W_Z = 9, NZW = 8;
 constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
-constexpr int HB = 4;                // weights / logits buffers (tiles in flight after the coefficients)
+constexpr int HB = 2;                // aggregation-weight buffers (tiles published ahead of the pre-aggregate)
+constexpr int HBL = 3;               // H_res logit buffers (the Sinkhorn warp takes tiles in pairs)
+// Optional explicit limit: the x stream may run at most Z_LAG tiles ahead of
+// this CTA's pre-aggregate (0 = off).  The weights buffers already bound the
+// lead: the coefficient warp publishes tile lt only after tile lt-HB is
+// aggregated everywhere.
+#ifndef MHC_TC_ZLAG
+#define MHC_TC_ZLAG 0
+#endif
+constexpr int Z_LAG = MHC_TC_ZLAG;
+static_assert(Z_LAG <= HB, "the producer's ZD wait must not skip a phase");
 // TMEM per accumulator buffer: projection (NB <= 64 columns) at +0, the Gram
 // block x . x^T of the chunk rows (128 columns) after it; two buffers.
 constexpr int ACC_STRIDE = 256, TMEM_COLS = 512;
@@ -81,6 +91,8 @@ __device__ long long g_trace[64][32];
 #define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = clock64(); } while (0)
 __device__ long long g_trace_ch[64][8][8];
 #define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = clock64(); } while (0)
+__device__ long long g_trace_z[64][8][4];  // per tile, per box: issue, land, processed
+#define TC_TRACE_Z(b, k) do { if (cid == 0 && rank == 0 && lt < 64 && (b) < 8) g_trace_z[lt][b][k] = clock64(); } while (0)
 // global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
 __device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -96,6 +108,7 @@ __device__ unsigned long long g_trace_cta[256][2];  // per CTA: loop start, loop
 #define TC_MARK(i) do { } while (0)
 #define TC_TRACE(ev) do { } while (0)
 #define TC_TRACE_CH(c, k) do { } while (0)
+#define TC_TRACE_Z(b, k) do { } while (0)
 #endif
 enum TraceEv { T_P_FIRST, T_P_LAST, T_M_ACCE, T_M_COMMIT, T_R_FULL0, T_R_ACCF, T_R_INE, T_R_PUSHED, T_C_INF,
                T_C_HPE, T_C_PUSHED, T_Z_BOX3, T_Z_HPF, T_SK_LGF, T_SK_DONE, T_Z_BOX0, T_Z_DONE, T_ZP_GO, T_C_LGE };
@@ -118,8 +131,8 @@ struct Layout {
 // barrier slots
 constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ZF = 2 * RING_MAX, B_ZE = B_ZF + ZS_MAX, B_ACCF = B_ZE + ZS_MAX,
               B_ACCE = B_ACCF + 2, B_INF = B_ACCE + 2, B_INE = B_INF + IN_BUFS, B_HPF = B_INE + IN_BUFS,
-              B_HPE = B_HPF + HB, B_ZD = B_HPE + HB, B_ZGO = B_ZD + HB, B_LGF = B_ZGO + HB, B_LGE = B_LGF + HB,
-              B_DRAIN = B_LGE + HB, B_PHI = B_DRAIN + 1, NBARS = B_PHI + 1;
+              B_HPE = B_HPF + HB, B_ZD = B_HPE + HB, B_ZGO = B_ZD + HB, B_LGF = B_ZGO + HB, B_LGE = B_LGF + HBL,
+              B_DRAIN = B_LGE + HBL, B_PHI = B_DRAIN + 1, NBARS = B_PHI + 1;
 // warps that convert phi / load the parameters in the prologue (all but the
 // producers and the MMA issuer, which start streaming x at once)
 constexpr int W_CONV = W_MMA + 1, NCONV = NWARPS - W_CONV;
@@ -142,7 +155,7 @@ __host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, 
   L.zbuf = o;  o += (uint32_t)ZS * zbox;
   L.inbox = o; o += (uint32_t)IN_BUFS * S * TPC * IBS * 4;
   L.hp = o;    o += (uint32_t)HB * TM * HPN * 4;
-  L.lg = o;    o += (uint32_t)HB * TPC * 16 * 4;   // H_res logits of the CTA's own tokens (n <= 4)
+  L.lg = o;    o += (uint32_t)HBL * TPC * 16 * 4;  // H_res logits of the CTA's own tokens (n <= 4)
   L.par = o;   o += ((NPAR * 4 + 15) / 16) * 16;
   L.bar = o;   o += NBARS * 8;
   L.tmem = o;  o += 4;
@@ -250,6 +263,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       mbar_init(BAR(B_HPE + b), S);        // one per CTA (its pre-aggregate is done)
       mbar_init(BAR(B_ZD + b), NZW);       // local: pre-aggregate warps done
       mbar_init(BAR(B_ZGO + b), 1);        // local: tile's projections complete cluster-wide
+    }
+    for (int b = 0; b < HBL; ++b) {
       mbar_init(BAR(B_LGF + b), 1);        // local: logits of the CTA's tokens written
       mbar_init(BAR(B_LGE + b), 1);        // local: Sinkhorn warp done with the logits
     }
@@ -351,10 +366,18 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   if (warp == W_PROD) {
     if (lane == 0) {
       // ---------------- x chunk producer ----------------
+      // x is read a second time (from L2) by the pre-aggregate a few tiles
+      // later: keep it with high L2 priority until then
+      const uint64_t keep = l2_policy_evict_last();
       uint32_t q = 0;
       int lt = 0;
       bool ok = true;
       for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+        if (Z_LAG > 0 && lt >= Z_LAG &&
+            !wait_parity<false>(BAR(B_ZD + (lt - Z_LAG) % HB), (uint32_t)((lt - Z_LAG) / HB) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
@@ -362,8 +385,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
           if (c == 0) TC_TRACE(T_P_FIRST);
           if (c == CH - 1) TC_TRACE(T_P_LAST);
           mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
-          tma_load_2d(base_u32 + L.ring + slot * SLOT + XOFF, &tmap, (int)rank * a.KS + c * 64, tile * TM,
-                      BAR(B_FULL + slot));
+          tma_load_2d_hint(base_u32 + L.ring + slot * SLOT + XOFF, &tmap, (int)rank * a.KS + c * 64, tile * TM,
+                           BAR(B_FULL + slot), keep);
         }
       }
       if (!ok) record_error(ERR_PROD, abort_flag);
@@ -375,6 +398,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   } else if (warp == W_ZPROD) {
     if (lane == 0) {
       // ---------------- pre-aggregate box producer ----------------
+      // last use of these x lines: demote them
+      const uint64_t drop = l2_policy_evict_first();
       const int cz = a.C / S;
       uint32_t zq = 0;
       int lt = 0;
@@ -387,9 +412,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         for (int qq = 0; qq < TM / a.ZR; ++qq, ++zq) {
           const uint32_t slot = zq % ZS, zph = (zq / ZS) & 1u;
           if (!wait_parity<false>(BAR(B_ZE + slot), zph ^ 1u, abort_flag)) { ok = false; break; }
+          TC_TRACE_Z(qq, 0);
           mbar_arrive_expect_tx(BAR(B_ZF + slot), (uint32_t)a.zbox);
-          tma_load_3d(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0, tile * TM + qq * a.ZR,
-                      BAR(B_ZF + slot));
+          tma_load_3d_hint(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0,
+                           tile * TM + qq * a.ZR, BAR(B_ZF + slot), drop);
         }
       }
       if (!ok) record_error(ERR_PROD, abort_flag);
@@ -543,9 +569,10 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       // pre-aggregate loads.  Signalled only after tile lt-HB is done everywhere,
       // so the box producer never sees two phases of ZGO[hb] at once.
       if (lane == 0) mbar_arrive(BAR(B_ZGO + hb));
-      // and the logits buffer must be free (Sinkhorn of tile lt-HB done)
+      // and the logits buffer must be free (Sinkhorn of tile lt-HBL done)
+      const int lb = lt % HBL;
       if constexpr (MODE == FULL) {
-        if (!WAIT_WARP(false, BAR(B_LGE + hb), hph ^ 1u)) { ok = false; break; }
+        if (!WAIT_WARP(false, BAR(B_LGE + lb), ((uint32_t)(lt / HBL) & 1u) ^ 1u)) { ok = false; break; }
         if (lane == 0) TC_TRACE(T_C_LGE);
       }
       if (lane < TPC) {
@@ -559,7 +586,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
             ho[i] = sigmoidf_(__fadd_rn(__fmul_rn(m[N + i], par[1]), par[3 + N + i])) * a.p.post_mult;
         }
         if constexpr (MODE == FULL) {
-          float *lrow = lg + (hb * TPC + lane) * 16;
+          float *lrow = lg + (lb * TPC + lane) * 16;
 #pragma unroll
           for (int k = 0; k < N * N; ++k) lrow[k] = __fadd_rn(__fmul_rn(m[2 * N + k], par[2]), par[3 + 2 * N + k]);
         }
@@ -577,7 +604,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       if (lane == 0) TC_TRACE(T_C_PUSHED);
       if constexpr (MODE == FULL) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(B_LGF + hb));  // logits ready for the Sinkhorn warp
+        if (lane == 0) mbar_arrive(BAR(B_LGF + lb));  // logits ready for the Sinkhorn warp
       }
       // per-token outputs
       if (live) {
@@ -604,13 +631,13 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       bool ok = true;
       for (int tile = (int)cid; tile < ntiles && ok; tile += 2 * (int)ncl, lt += 2) {
         const bool two = tile + (int)ncl < ntiles;
-        if (!WAIT_WARP(false, BAR(B_LGF + lt % HB), (uint32_t)(lt / HB) & 1u)) { ok = false; break; }
-        if (two && !WAIT_WARP(false, BAR(B_LGF + (lt + 1) % HB), (uint32_t)((lt + 1) / HB) & 1u)) {
+        if (!WAIT_WARP(false, BAR(B_LGF + lt % HBL), (uint32_t)(lt / HBL) & 1u)) { ok = false; break; }
+        if (two && !WAIT_WARP(false, BAR(B_LGF + (lt + 1) % HBL), (uint32_t)((lt + 1) / HBL) & 1u)) {
           ok = false;
           break;
         }
         TC_TRACE(T_SK_LGF);
-        const int my_lt = lt + half, hb = my_lt % HB;
+        const int my_lt = lt + half, hb = my_lt % HBL;
         const int64_t tok = (int64_t)(tile + half * (int)ncl) * TM + (int)rank * TPC + (lane & 15);
         if ((half == 0 || two) && tok < a.T) {
           float hm[N * N];
@@ -625,8 +652,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         __syncwarp();
         TC_TRACE(T_SK_DONE);
         if (lane == 0) {
-          mbar_arrive(BAR(B_LGE + lt % HB));  // logits buffers free
-          if (two) mbar_arrive(BAR(B_LGE + (lt + 1) % HB));
+          mbar_arrive(BAR(B_LGE + lt % HBL));  // logits buffers free
+          if (two) mbar_arrive(BAR(B_LGE + (lt + 1) % HBL));
         }
       }
       if (!ok) record_error(ERR_SK, abort_flag);
@@ -657,6 +684,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         const uint32_t slot = zq % ZS;
         if (!WAIT_WARP(false, BAR(B_ZF + slot), (zq / ZS) & 1u)) { ok = false; break; }
         if (warp == W_Z && lane == 0 && qq == 0) TC_TRACE(T_Z_BOX0);
+        if (warp == W_Z && lane == 0) TC_TRACE_Z(qq, 1);
         if (warp == W_Z && lane == 0 && qq == TM / ZR - 1) TC_TRACE(T_Z_BOX3);
         const uint8_t *box = base + L.zbuf + slot * (uint32_t)a.zbox;
         const int64_t t0 = (int64_t)tile * TM + qq * ZR;  // first token of the box
@@ -697,6 +725,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
         }
         // the box may be refilled (read-then-overwrite: the arrive orders it)
         __syncwarp();
+        if (warp == W_Z && lane == 0) TC_TRACE_Z(qq, 2);
         if (lane == 0) mbar_arrive(BAR(B_ZE + slot));
       }
       if (!ok) break;
