@@ -7,10 +7,7 @@
 //
 //   warp 0      TMA producer: 128 x 64 bf16 chunks of its x K-slice into a
 //               ring (128-byte swizzle, 16 KB per slot).
-//   warp 1      pre-aggregate producer: once every CTA of the cluster has
-//               finished a tile's projection (so the tile's x is in L2), TMA
-//               boxes of 32 tokens x n streams x C/8 columns (3-D tensor map).
-//   warp 2      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
+//   warp 1      tcgen05 MMA issuer: D[128 tok, NB] += x_chunk . phi_slice^T
 //               (M = 128, K = 16 per instruction) into a double-buffered TMEM
 //               accumulator.  phi is split once per launch into bf16 hi | lo
 //               halves (NB = 2*FD padded to 16) held in shared memory for the
@@ -18,21 +15,26 @@
 //               same chunk is also multiplied by itself (G += x . x^T, N = 128):
 //               the diagonal of G is each row's sum of squares, so no thread
 //               reads the x ring and a slot is free as soon as its MMAs retire.
-//   warps 3-6   row warps (thread = token row = TMEM lane): the slice's
+//   warps 2-5   row warps (thread = token row = TMEM lane): the slice's
 //               partial projection and sum of squares from TMEM; the (FD
 //               partials, sum of squares) row is pushed with st.async into the
 //               inbox of the CTA that owns the token (the stores complete the
 //               owner's mbarrier themselves).
-//   warp 7      coefficient warp: sums the 8 slices in a fixed order
+//   warp 6      coefficient warp: sums the 8 slices in a fixed order
 //               (deterministic), applies 1/rms, the sigmoid gates and the
 //               H_res affine map, pushes the fp32 aggregation weights to all 8
 //               CTAs with st.async and writes the per-token outputs.
-//   warp 8      Sinkhorn warp: H_res of the CTA's 16 tokens of two tiles at
+//   warp 7      Sinkhorn warp: H_res of the CTA's 16 tokens of two tiles at
 //               a time (one token per lane, matrix in registers).  The logits
 //               are 3-deep buffered, so the 20 iterations stay off the tile's
 //               critical path.
-//   warps 9-16  pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] from the
-//               staged boxes, fp32 accumulation in packed pairs.
+//   warps 8-    pre-aggregate: z[t, c] = sum_i w[t,i] x[t, i*C + c] for the
+//               CTA's C/8 columns.  Once every CTA of the cluster has
+//               finished a tile's projection (so the tile's x is in L2) each
+//               thread loads its items straight from L2 with 16-byte LDGs
+//               (16 loads in flight per thread, no shared-memory staging: the
+//               SM's TMA path is already busy with the x stream), then waits
+//               for the weights and accumulates in fp32 packed pairs.
 //
 // All hand-offs are mbarriers.  There is no named barrier, no cluster barrier
 // and no cluster-scope fence inside the tile loop, and every wait is bounded
@@ -58,16 +60,19 @@ using namespace sm100;
 
 constexpr int S = 8;                 // CTAs per cluster (K split)
 constexpr int TM = 128;              // tokens per tile (UMMA M)
-constexpr int RING_MAX = 8;          // x chunk slots (runtime count <= this)
-constexpr int ZS_MAX = 8;            // pre-aggregate box slots (runtime count <= this)
+constexpr int RING_MAX = 12;         // x chunk slots (runtime count <= this)
 // tokens per pre-aggregate box: 32 or 16 (a quarter or an eighth of a tile),
 // chosen with the number of boxes in flight to fit shared memory
 constexpr int CHUNK = TM * 128;      // 128 rows x 128 bytes
 constexpr int TPC = TM / S;          // tokens whose coefficients a CTA finalises
-constexpr int NWARPS = 17, NTHREADS = NWARPS * 32;
+#ifndef MHC_TC_NZW
+#define MHC_TC_NZW 12
+#endif
+constexpr int NZW = MHC_TC_NZW;   // pre-aggregate warps
+constexpr int NWARPS = 8 + NZW, NTHREADS = NWARPS * 32;
 // Each producer / issuer has a warp of its own: a lane that waits on an
 // mbarrier holds up every other branch of its warp.
-constexpr int W_PROD = 0, W_ZPROD = 1, W_MMA = 2, W_ROW = 3, W_COEF = 7, W_SK = 8, W_Z = 9, NZW = 8;
+constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_SK = 7, W_Z = 8;
 constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
 constexpr int HB = 2;                // aggregation-weight buffers (tiles published ahead of the pre-aggregate)
 constexpr int HBL = 3;               // H_res logit buffers (the Sinkhorn warp takes tiles in pairs)
@@ -91,8 +96,6 @@ __device__ long long g_trace[64][32];
 #define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = clock64(); } while (0)
 __device__ long long g_trace_ch[64][8][8];
 #define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = clock64(); } while (0)
-__device__ long long g_trace_z[64][8][4];  // per tile, per box: issue, land, processed
-#define TC_TRACE_Z(b, k) do { if (cid == 0 && rank == 0 && lt < 64 && (b) < 8) g_trace_z[lt][b][k] = clock64(); } while (0)
 // global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
 __device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -108,7 +111,6 @@ __device__ unsigned long long g_trace_cta[256][2];  // per CTA: loop start, loop
 #define TC_MARK(i) do { } while (0)
 #define TC_TRACE(ev) do { } while (0)
 #define TC_TRACE_CH(c, k) do { } while (0)
-#define TC_TRACE_Z(b, k) do { } while (0)
 #endif
 enum TraceEv { T_P_FIRST, T_P_LAST, T_M_ACCE, T_M_COMMIT, T_R_FULL0, T_R_ACCF, T_R_INE, T_R_PUSHED, T_C_INF,
                T_C_HPE, T_C_PUSHED, T_Z_BOX3, T_Z_HPF, T_SK_LGF, T_SK_DONE, T_Z_BOX0, T_Z_DONE, T_ZP_GO, T_C_LGE };
@@ -125,11 +127,11 @@ struct Cfg {
 };
 
 struct Layout {
-  uint32_t ring, phi, zbuf, inbox, hp, lg, par, bar, tmem, abort, total;
+  uint32_t ring, phi, inbox, hp, lg, par, bar, tmem, abort, total;
 };
 
 // barrier slots
-constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ZF = 2 * RING_MAX, B_ZE = B_ZF + ZS_MAX, B_ACCF = B_ZE + ZS_MAX,
+constexpr int B_FULL = 0, B_EMPTY = RING_MAX, B_ACCF = 2 * RING_MAX,
               B_ACCE = B_ACCF + 2, B_INF = B_ACCE + 2, B_INE = B_INF + IN_BUFS, B_HPF = B_INE + IN_BUFS,
               B_HPE = B_HPF + HB, B_ZD = B_HPE + HB, B_ZGO = B_ZD + HB, B_LGF = B_ZGO + HB, B_LGE = B_LGF + HBL,
               B_DRAIN = B_LGE + HBL, B_PHI = B_DRAIN + 1, NBARS = B_PHI + 1;
@@ -146,13 +148,11 @@ __host__ __device__ inline uint32_t slot_bytes(int merged, int NB) {
   return (uint32_t)CHUNK + (merged ? (uint32_t)NB * 128 : 0u);
 }
 
-__host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR, int RING, int ZS,
-                                              int zbox, int merged) {
+__host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, int NPAR, int RING, int merged) {
   Layout L;
   uint32_t o = 0;
   L.ring = o;  o += (uint32_t)RING * slot_bytes(merged, NB);
   L.phi = o;   o += merged ? 0u : (uint32_t)CH * NB * 128;
-  L.zbuf = o;  o += (uint32_t)ZS * zbox;
   L.inbox = o; o += (uint32_t)IN_BUFS * S * TPC * IBS * 4;
   L.hp = o;    o += (uint32_t)HB * TM * HPN * 4;
   L.lg = o;    o += (uint32_t)HBL * TPC * 16 * 4;  // H_res logits of the CTA's own tokens (n <= 4)
@@ -167,9 +167,8 @@ __host__ __device__ inline Layout make_layout(int CH, int NB, int IBS, int HPN, 
 struct Args {
   int64_t T;
   int C, nC, KS, CH;
-  int RING, ZS, zbox;   // x ring slots, pre-aggregate box slots, box bytes
+  int RING;             // x ring slots
   int merged;           // operand layout (see make_layout)
-  int ZR;               // tokens per pre-aggregate box
   const void *phi;
   CoefParams p;
   __nv_bfloat16 *z;
@@ -207,16 +206,15 @@ __device__ __forceinline__ void load_params_tc(float *par, const CoefParams &p, 
 
 template <int N, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap zmap,
-              const __nv_bfloat16 *__restrict__ x, Args a) {
+pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__restrict__ x, Args a) {
   using Cf = Cfg<N, MODE>;
   constexpr int FD = Cf::FD, NB = Cf::NB, IBS = Cf::IBS, NPAR = Cf::NPAR, HPN = Cf::HPN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t *base = smem_raw + (base_u32 - raw_u32);
-  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR, a.RING, a.ZS, a.zbox, a.merged);
-  const int RING = a.RING, ZS = a.ZS;
+  const Layout L = make_layout(a.CH, NB, IBS, HPN, NPAR, a.RING, a.merged);
+  const int RING = a.RING;
   const uint32_t SLOT = slot_bytes(a.merged, NB);
   const uint32_t XOFF = a.merged ? (uint32_t)NB * 128u : 0u;  // x chunk offset inside a slot
   const uint32_t GRAM = a.merged ? (uint32_t)NB : 64u;         // Gram block column in the accumulator
@@ -246,10 +244,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       mbar_init(BAR(B_FULL + i), 1);
       mbar_init(BAR(B_EMPTY + i), 1);      // MMA commit
     }
-    for (int i = 0; i < ZS; ++i) {
-      mbar_init(BAR(B_ZF + i), 1);
-      mbar_init(BAR(B_ZE + i), NZW);       // every pre-aggregate warp
-    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(B_ACCF + b), 1);
       mbar_init(BAR(B_ACCE + b), 4);
@@ -262,7 +256,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       mbar_init(BAR(B_HPF + b), 1);        // armed by the pre-aggregate warps; st.async bytes complete it
       mbar_init(BAR(B_HPE + b), S);        // one per CTA (its pre-aggregate is done)
       mbar_init(BAR(B_ZD + b), NZW);       // local: pre-aggregate warps done
-      mbar_init(BAR(B_ZGO + b), 1);        // local: tile's projections complete cluster-wide
+      mbar_init(BAR(B_ZGO + b), 1);        // local: tile's projections complete cluster-wide (x in L2)
     }
     for (int b = 0; b < HBL; ++b) {
       mbar_init(BAR(B_LGF + b), 1);        // local: logits of the CTA's tokens written
@@ -366,7 +360,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
   if (warp == W_PROD) {
     if (lane == 0) {
       // ---------------- x chunk producer ----------------
-      // x is read a second time (from L2) by the pre-aggregate a few tiles
+      // x is read a second time (from L2) by the pre-aggregate a few µs
       // later: keep it with high L2 priority until then
       const uint64_t keep = l2_policy_evict_last();
       uint32_t q = 0;
@@ -393,34 +387,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       // copies in flight must land before the CTA can exit
       const uint32_t q0 = q > (uint32_t)RING ? q - RING : 0u;
       for (uint32_t p = q0; p < q; ++p) wait_parity<false>(BAR(B_FULL + p % RING), (p / RING) & 1u, nullptr);
-    }
-    __syncwarp();
-  } else if (warp == W_ZPROD) {
-    if (lane == 0) {
-      // ---------------- pre-aggregate box producer ----------------
-      // last use of these x lines: demote them
-      const uint64_t drop = l2_policy_evict_first();
-      const int cz = a.C / S;
-      uint32_t zq = 0;
-      int lt = 0;
-      bool ok = true;
-      for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
-        const int hb = lt % HB;
-        const uint32_t hph = (uint32_t)(lt / HB) & 1u;
-        if (!wait_parity<false>(BAR(B_ZGO + hb), hph, abort_flag)) { ok = false; break; }
-        TC_TRACE(T_ZP_GO);
-        for (int qq = 0; qq < TM / a.ZR; ++qq, ++zq) {
-          const uint32_t slot = zq % ZS, zph = (zq / ZS) & 1u;
-          if (!wait_parity<false>(BAR(B_ZE + slot), zph ^ 1u, abort_flag)) { ok = false; break; }
-          TC_TRACE_Z(qq, 0);
-          mbar_arrive_expect_tx(BAR(B_ZF + slot), (uint32_t)a.zbox);
-          tma_load_3d_hint(base_u32 + L.zbuf + slot * (uint32_t)a.zbox, &zmap, (int)rank * cz, 0,
-                           tile * TM + qq * a.ZR, BAR(B_ZF + slot), drop);
-        }
-      }
-      if (!ok) record_error(ERR_PROD, abort_flag);
-      const uint32_t q0 = zq > (uint32_t)ZS ? zq - ZS : 0u;
-      for (uint32_t p = q0; p < zq; ++p) wait_parity<false>(BAR(B_ZF + p % ZS), (p / ZS) & 1u, nullptr);
     }
     __syncwarp();
   } else if (warp == W_MMA) {
@@ -567,7 +533,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
       if (lane == 0) TC_TRACE(T_C_HPE);
       // every CTA finished this tile's projection, so its x is in L2: start the
       // pre-aggregate loads.  Signalled only after tile lt-HB is done everywhere,
-      // so the box producer never sees two phases of ZGO[hb] at once.
+      // so no pre-aggregate warp can see two phases of ZGO[hb] at once.
       if (lane == 0) mbar_arrive(BAR(B_ZGO + hb));
       // and the logits buffer must be free (Sinkhorn of tile lt-HBL done)
       const int lb = lt % HBL;
@@ -660,42 +626,60 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
     }
   } else {
     // ---------------- pre-aggregate warps ----------------
+    constexpr int IPB = N >= 16 ? 1 : (16 / N < 4 ? 16 / N : 4);  // items per batch: <= 16 loads in flight
+    constexpr int ZT = NZW * 32;
     const int ztid = tid - W_Z * 32;
-    const int ZR = a.ZR;
     const int cz = a.C / S;      // columns of z owned by this CTA
     const int vpr = cz / 8;      // 16-byte vectors per row and stream
     const int c0 = (int)rank * cz;
-    const int zrow = N * cz * 2; // bytes per box token (N streams x cz columns)
-    // item (row r, vector v) walk of a box without divisions in the loop:
-    // thread starts at item ztid and steps by NZW*32 items
+    const int items = TM * vpr;  // (row, vector) items per tile
+    const int nbatch = (items + ZT * IPB - 1) / (ZT * IPB);
+    // item walk without divisions in the loop: thread starts at item ztid and
+    // steps by ZT items (row r, vector v)
     const int r_first = ztid / vpr, v_first = ztid - r_first * vpr;
-    const int r_step = (NZW * 32) / vpr, v_step = (NZW * 32) - r_step * vpr;
-    uint32_t zq = 0;             // boxes consumed so far
+    const int r_step = ZT / vpr, v_step = ZT - r_step * vpr;
     int lt = 0;
     bool ok = true;
     for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
       const int hb = lt % HB;
       const uint32_t hph = (uint32_t)(lt / HB) & 1u;
       if (warp == W_Z && lane == 0) mbar_arrive_expect_tx(BAR(B_HPF + hb), HP_TX);  // arm: 8 CTAs' weights
-      if (!WAIT_WARP(true, BAR(B_HPF + hb), hph)) { ok = false; break; }
-      if (warp == W_Z && lane == 0) TC_TRACE(T_Z_HPF);
+      // the tile's x is in L2 once every CTA has finished its projection
+      if (!WAIT_WARP(false, BAR(B_ZGO + hb), hph)) { ok = false; break; }
+      if (warp == W_Z && lane == 0) TC_TRACE(T_ZP_GO);
+      const int64_t t0 = (int64_t)tile * TM;
+      const int rows = a.T - t0 < TM ? (int)(a.T - t0) : TM;
+      const __nv_bfloat16 *xb = x + t0 * a.nC + c0;
+      __nv_bfloat16 *zb = a.z + t0 * a.C + c0;
       const float *hps = hp + hb * TM * HPN;
-      for (int qq = 0; qq < TM / ZR; ++qq, ++zq) {
-        const uint32_t slot = zq % ZS;
-        if (!WAIT_WARP(false, BAR(B_ZF + slot), (zq / ZS) & 1u)) { ok = false; break; }
-        if (warp == W_Z && lane == 0 && qq == 0) TC_TRACE(T_Z_BOX0);
-        if (warp == W_Z && lane == 0) TC_TRACE_Z(qq, 1);
-        if (warp == W_Z && lane == 0 && qq == TM / ZR - 1) TC_TRACE(T_Z_BOX3);
-        const uint8_t *box = base + L.zbuf + slot * (uint32_t)a.zbox;
-        const int64_t t0 = (int64_t)tile * TM + qq * ZR;  // first token of the box
-        const int rows = a.T - t0 < ZR ? (int)(a.T - t0) : ZR;
-        __nv_bfloat16 *zb = a.z + t0 * a.C + c0;
-        for (int r = r_first, v = v_first; r < rows;) {
-          const int t = qq * ZR + r;
+      int r = r_first, v = v_first;
+      for (int b = 0; b < nbatch; ++b) {
+        uint4 xv[IPB][N];
+        int rr[IPB], vv[IPB];
+#pragma unroll
+        for (int u = 0; u < IPB; ++u) {
+          rr[u] = r;
+          vv[u] = v;
+          if (r < rows) {
+            const __nv_bfloat16 *src = xb + (int64_t)r * a.nC + v * 8;
+#pragma unroll
+            for (int st = 0; st < N; ++st) xv[u][st] = __ldcs(reinterpret_cast<const uint4 *>(src + st * a.C));
+          }
+          r += r_step;
+          v += v_step;
+          if (v >= vpr) { v -= vpr; ++r; }
+        }
+        if (b == 0) {
+          if (!WAIT_WARP(true, BAR(B_HPF + hb), hph)) { ok = false; break; }
+          if (warp == W_Z && lane == 0) TC_TRACE(T_Z_HPF);
+        }
+#pragma unroll
+        for (int u = 0; u < IPB; ++u) {
+          if (rr[u] >= rows) continue;
           float wv[HPN];
 #pragma unroll
           for (int v4 = 0; v4 < HPN / 4; ++v4) {
-            const float4 q4 = *reinterpret_cast<const float4 *>(hps + t * HPN + 4 * v4);
+            const float4 q4 = *reinterpret_cast<const float4 *>(hps + rr[u] * HPN + 4 * v4);
             wv[4 * v4] = q4.x; wv[4 * v4 + 1] = q4.y; wv[4 * v4 + 2] = q4.z; wv[4 * v4 + 3] = q4.w;
           }
           // fp32 accumulation in packed pairs: acc[j] holds columns 2j, 2j+1
@@ -703,8 +687,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
 #pragma unroll
           for (int st = 0; st < N; ++st) {
             const uint64_t w2 = f2_pack(wv[st], wv[st]);
-            const uint4 xr = *reinterpret_cast<const uint4 *>(box + r * zrow + st * cz * 2 + v * 16);
-            const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
+            const uint32_t xw[4] = {xv[u][st].x, xv[u][st].y, xv[u][st].z, xv[u][st].w};
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               acc[j] = st == 0 ? f2_fma(w2, bf16x2_to_f2(xw[j]), f2_pack(0.f, 0.f))
@@ -718,15 +701,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ 
             const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
             ow[j] = *reinterpret_cast<const uint32_t *>(&h2);
           }
-          *reinterpret_cast<uint4 *>(zb + (int64_t)r * a.C + v * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-          r += r_step;
-          v += v_step;
-          if (v >= vpr) { v -= vpr; ++r; }
+          *reinterpret_cast<uint4 *>(zb + (int64_t)rr[u] * a.C + vv[u] * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
         }
-        // the box may be refilled (read-then-overwrite: the arrive orders it)
-        __syncwarp();
-        if (warp == W_Z && lane == 0) TC_TRACE_Z(qq, 2);
-        if (lane == 0) mbar_arrive(BAR(B_ZE + slot));
       }
       if (!ok) break;
       // this CTA is done reading the weights of `hb`: tell every writer
@@ -782,33 +758,27 @@ constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block
 // the merged layout with the longest ring (4..8 slots, a multiple of CH) and at
 // least two pre-aggregate boxes in flight, else the separate layout.
 template <int N, int MODE>
-static bool pick_slots(int CH, int C, Args &a) {
+static bool pick_slots(int CH, Args &a) {
   using Cf = Cfg<N, MODE>;
-  auto fits = [&](int r, int z, int zr, int m) {
-    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, r, z, zr * N * (C / S) * 2, m);
+  auto fits = [&](int r, int m) {
+    const Layout L = make_layout(CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, r, m);
     return (size_t)L.total + 1024 <= SMEM_LIMIT;
   };
-  auto take = [&](int r, int z, int zr, int m) {
+  auto take = [&](int r, int m) {
     a.RING = r;
-    a.ZS = z;
-    a.ZR = zr;
-    a.zbox = zr * N * (C / S) * 2;
     a.merged = m;
     return true;
   };
-#if defined(MHC_TC_RING) && defined(MHC_TC_ZS) && defined(MHC_TC_MERGED) && defined(MHC_TC_ZR)
-  return fits(MHC_TC_RING, MHC_TC_ZS, MHC_TC_ZR, MHC_TC_MERGED) && (!MHC_TC_MERGED || MHC_TC_RING % CH == 0) &&
-         take(MHC_TC_RING, MHC_TC_ZS, MHC_TC_ZR, MHC_TC_MERGED);
+#if defined(MHC_TC_RING) && defined(MHC_TC_MERGED)
+  return fits(MHC_TC_RING, MHC_TC_MERGED) && (!MHC_TC_MERGED || MHC_TC_RING % CH == 0) &&
+         take(MHC_TC_RING, MHC_TC_MERGED);
 #else
-  // pre-aggregate (tokens per box, boxes in flight): quarter-tile boxes first
-  const int zopts[][2] = {{32, 3}, {32, 2}, {16, 4}, {16, 3}};
-  for (int r = (RING_MAX / CH) * CH; r >= 4; r -= CH)
-    for (const auto &zo : zopts)
-      if (fits(r, zo[1], zo[0], 1)) return take(r, zo[1], zo[0], 1);
-  const int prefs[][2] = {{5, 3}, {4, 4}, {6, 2}, {4, 3}, {4, 2}, {3, 2}};
-  for (const auto &pr : prefs)
-    for (int zr : {32, 16})
-      if (fits(pr[0], pr[1], zr, 0)) return take(pr[0], pr[1], zr, 0);
+  // the merged layout with a ring of 6..8 slots (a multiple of CH), else the
+  // separate layout with the longest ring that fits
+  for (int r = (8 / CH) * CH; r >= 6; r -= CH)
+    if (fits(r, 1)) return take(r, 1);
+  for (int r = 8; r >= 4; --r)
+    if (fits(r, 0)) return take(r, 0);
   return false;
 #endif
 }
@@ -820,8 +790,8 @@ static bool pick_slots(int CH, int C, Args &a) {
 struct MapEntry {
   const void *x;
   int64_t T;
-  int C, N, ZR, dev;
-  CUtensorMap tmap, zmap;
+  int C, N, dev;
+  CUtensorMap tmap;
 };
 struct KernEntry {
   const void *kern;
@@ -836,41 +806,25 @@ static int g_maps_n = 0, g_maps_next = 0;
 static KernEntry g_kerns[64];
 static int g_kerns_n = 0;
 
-static bool encode_maps(const void *x, int64_t T, int C, int N, int ZR, CUtensorMap &tmap, CUtensorMap &zmap) {
+static bool encode_map(const void *x, int64_t T, int C, int N, CUtensorMap &tmap) {
   auto enc = encode_fn();
   if (!enc) return false;
   const int nC = N * C;
   // x as (T rows) x (nC columns): 128-row x 64-column K chunks, 128-byte swizzle
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
-    const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)TM};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return false;
-  }
-  // x as (T) x (n streams) x (C columns): boxes of ZR tokens x n streams x C/8 columns
-  {
-    const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)N, (cuuint64_t)T};
-    const cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)nC * 2};
-    const cuuint32_t box[3] = {(cuuint32_t)(C / S), (cuuint32_t)N, (cuuint32_t)ZR};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    if (enc(&zmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return false;
-  }
-  return true;
+  const cuuint64_t dims[2] = {(cuuint64_t)nC, (cuuint64_t)T};
+  const cuuint64_t strides[1] = {(cuuint64_t)nC * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)TM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int N, int MODE>
 static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaStream_t stream) {
   using Cf = Cfg<N, MODE>;
-  if (!pick_slots<N, MODE>(args.CH, C, args)) return cudaErrorNotSupported;
-  const Layout L =
-      make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.ZS, args.zbox, args.merged);
+  if (!pick_slots<N, MODE>(args.CH, args)) return cudaErrorNotSupported;
+  const Layout L = make_layout(args.CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, args.RING, args.merged);
   const size_t smem = (size_t)L.total + 1024;
   auto kern = pre_tc_kernel<N, MODE>;
   int dev = 0;
@@ -891,7 +845,7 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
 
-  CUtensorMap tmap, zmap;
+  CUtensorMap tmap;
   int max_clusters = 0;
   {
     std::lock_guard<std::mutex> lock(g_host_mu);
@@ -921,31 +875,28 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
 
     int hit = -1;
     for (int i = 0; i < g_maps_n; ++i)
-      if (g_maps[i].x == x && g_maps[i].T == T && g_maps[i].C == C && g_maps[i].N == N && g_maps[i].ZR == args.ZR &&
-          g_maps[i].dev == dev)
+      if (g_maps[i].x == x && g_maps[i].T == T && g_maps[i].C == C && g_maps[i].N == N && g_maps[i].dev == dev)
         hit = i;
     if (hit < 0) {
       MapEntry &m = g_maps[g_maps_next];
-      if (!encode_maps(x, T, C, N, args.ZR, m.tmap, m.zmap)) return cudaErrorNotSupported;
+      if (!encode_map(x, T, C, N, m.tmap)) return cudaErrorNotSupported;
       m.x = x;
       m.T = T;
       m.C = C;
       m.N = N;
-      m.ZR = args.ZR;
       m.dev = dev;
       hit = g_maps_next;
       g_maps_next = (g_maps_next + 1) % 8;
       if (g_maps_n < 8) ++g_maps_n;
     }
     tmap = g_maps[hit].tmap;
-    zmap = g_maps[hit].zmap;
   }
 
   const int64_t ntiles = (T + TM - 1) / TM;
   const int clusters = (int)(ntiles < max_clusters ? ntiles : max_clusters);
   cfg.gridDim = dim3((unsigned)(clusters * S), 1, 1);
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, zmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, reinterpret_cast<const __nv_bfloat16 *>(x), args);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -977,10 +928,7 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
   a.KS = n * C / tc::S;
   a.CH = a.KS / 64;
   a.RING = 0;
-  a.ZS = 0;
-  a.zbox = 0;
   a.merged = 0;
-  a.ZR = 32;
   a.phi = phi;
   a.p = p;
   a.z = reinterpret_cast<__nv_bfloat16 *>(z);
