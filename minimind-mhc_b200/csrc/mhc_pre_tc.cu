@@ -73,7 +73,10 @@ constexpr int NWARPS = 8 + NZW, NTHREADS = NWARPS * 32;
 // Each producer / issuer has a warp of its own: a lane that waits on an
 // mbarrier holds up every other branch of its warp.
 constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_SK = 7, W_Z = 8;
-constexpr int IN_BUFS = 1;           // inbox buffers (partial rows from the 8 K slices)
+#ifndef MHC_TC_INBUFS
+#define MHC_TC_INBUFS 1
+#endif
+constexpr int IN_BUFS = MHC_TC_INBUFS;  // inbox buffers (partial rows from the 8 K slices)
 constexpr int HB = 2;                // aggregation-weight buffers (tiles published ahead of the pre-aggregate)
 constexpr int HBL = 3;               // H_res logit buffers (the Sinkhorn warp takes tiles in pairs)
 // Optional explicit limit: the x stream may run at most Z_LAG tiles ahead of
@@ -89,20 +92,20 @@ static_assert(Z_LAG <= HB, "the producer's ZD wait must not skip a phase");
 // block x . x^T of the chunk rows (128 columns) after it; two buffers.
 constexpr int ACC_STRIDE = 256, TMEM_COLS = 512;
 
-// Per-tile timeline instrumentation (clock64 of cluster 0, CTA 0), compiled in
+// Per-tile timeline instrumentation (global timer, cluster 0 / CTA 0), compiled in
 // only with -DMHC_TC_TRACE; events are indexed [local tile][event].
 #ifdef MHC_TC_TRACE
-__device__ long long g_trace[64][32];
-#define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = clock64(); } while (0)
-__device__ long long g_trace_ch[64][8][8];
-#define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = clock64(); } while (0)
-// global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
-__device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+__device__ long long g_trace[64][32];
+#define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = (long long)gtimer(); } while (0)
+__device__ long long g_trace_ch[64][8][8];
+#define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = (long long)gtimer(); } while (0)
+// global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
+__device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
 __device__ unsigned long long g_trace_cta[256][2];  // per CTA: loop start, loop end
 #define TC_MARK(i) do { if (threadIdx.x == 0) { const unsigned long long now_ = gtimer(); \
   if ((i) == 0) atomicMin(&g_trace_ns[0], now_); else atomicMax(&g_trace_ns[i], now_); \
