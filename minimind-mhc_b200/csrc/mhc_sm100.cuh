@@ -141,7 +141,7 @@ __device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
 
 // ---- TMA ----------------------------------------------------------------------
 // 2-D tiled load of one box into this CTA's shared memory, completing `bar`'s
-// transaction count.  (No multicast.)
+// transaction count (this CTA's shared memory only).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -160,29 +160,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-// 2-D tiled load with an L2 eviction-priority hint (no multicast).
+// 2-D tiled load with an L2 eviction-priority hint.
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void *tmap, int x, int y, uint32_t bar,
                                                  uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%2, %3}], [%4], %5;"
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
-      : "memory");
-}
-
-// 3-D tiled load (innermost coordinate first), no multicast.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int x, int y, int z, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void *tmap, int x, int y, int z, uint32_t bar,
-                                                 uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4}], [%5], %6;"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
       : "memory");
 }
 
