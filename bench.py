@@ -52,6 +52,57 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _time_backward(L, nat, x, ps, with_res, iters, z, h_post, h_res, inv_rms, mixes, f_out, t, n, c, fd, dev,
+                   sptr, stream, steps, peak_of):
+    """Backward of one layer through the C-ABI: mhc_post_bwd (merge) then
+    mhc_pre_bwd (coefficients, Sinkhorn by recompute, RMSNorm, dphi / dalpha /
+    dbias reductions).  dz stands in for the sublayer's input gradient.
+    Algorithmic bytes per token s*(6nC + 3C)."""
+    gen = torch.Generator(device=dev).manual_seed(99)
+    dout = torch.randn(t, n * c, device=dev, dtype=torch.bfloat16, generator=gen)
+    dz = torch.randn(t, c, device=dev, dtype=torch.bfloat16, generator=gen)
+    dx_post = torch.empty_like(x)
+    dx = torch.empty_like(x)
+    dh_res = torch.empty(t, n * n, device=dev) if with_res else None
+    dh_post = torch.empty(t, n, device=dev)
+    df = torch.empty_like(f_out)
+    gps = [torch.empty_like(p, dtype=torch.float32) for p in ps]
+    g_res = (gps[5], gps[6]) if with_res else (None, None)
+    a_res, b_res = (ps[5], ps[6]) if with_res else (None, None)
+    ws = nat.workspace(L.mhc_pre_bwd_workspace(t, n, c, int(with_res), int(with_res), iters), dev)
+
+    def step():
+        st = L.mhc_post_bwd(nat.ptr(dout), nat.ptr(x), nat.BF16, nat.ptr(h_res), nat.F32, nat.ptr(h_post),
+                            nat.F32, nat.ptr(f_out), nat.BF16, nat.ptr(dx_post), nat.ptr(dh_res), nat.ptr(dh_post),
+                            nat.ptr(df), t, n, c, sptr)
+        nat.check(st, "mhc_post_bwd")
+        st = L.mhc_pre_bwd(nat.ptr(x), nat.BF16, t, n, c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]),
+                           nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32,
+                           int(with_res), int(with_res), iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(inv_rms),
+                           nat.ptr(mixes), nat.ptr(dz), None, nat.ptr(dh_post), nat.ptr(dh_res), nat.F32,
+                           nat.ptr(dx_post), nat.ptr(dx), nat.ptr(gps[0]), nat.ptr(gps[1]), nat.ptr(gps[2]),
+                           nat.ptr(gps[3]), nat.ptr(gps[4]), nat.ptr(g_res[0]), nat.ptr(g_res[1]), nat.ptr(ws),
+                           ws.numel(), sptr)
+        nat.check(st, "mhc_pre_bwd")
+
+    for _ in range(3):
+        step()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    for e0, e1 in ev:
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sorted(e0.elapsed_time(e1) for e0, e1 in ev)[len(ev) // 2]
+    bytes_tok = 2 * (6 * n * c + 3 * c)
+    peak, kind = peak_of()
+    gbs = bytes_tok * t / (ms / 1e3) / 1e9
+    return {"ms_per_step": ms, "tokens_per_s": t / (ms / 1e3), "algorithmic_bytes_per_token": bytes_tok,
+            "gbs": gbs, "frac_of_measured": gbs / peak, "steps": steps,
+            "calls": "mhc_post_bwd + mhc_pre_bwd (median step, CUDA events)"}
+
+
 def _profiled_traffic(kernel, n, c, t, with_res):
     """DRAM bytes (read + write) per launch of the dominant kernel, from the
     committed ncu summary of this exact workload (profiles/*.md carries a line
@@ -299,6 +350,12 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total_ms = tt.item()
 
+    # ---- backward of the layer (training config), reported beside the forward --
+    bwd = None
+    if not args.no_bwd:
+        bwd = _time_backward(L, nat, x, ps, with_res, iters, z, h_post, h_res, inv_rms, mixes, f_out,
+                             t, n, c, fd, dev, sptr, stream, max(3, min(args.steps, 20)), peak_of=_peaks)
+
     # ---- end to end through the public API with host buffers -------------------
     e2e = None
     if not args.no_e2e:
@@ -383,6 +440,7 @@ def run_ours(args, rank, world, local_rank):
                      "traffic_source": traffic[1] if traffic else None,
                      "algorithmic_bytes_per_launch": d_bytes},
         "cpu_baseline": cpu,
+        "backward": bwd,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
@@ -403,6 +461,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-bwd", action="store_true", help="skip the backward measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

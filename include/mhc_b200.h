@@ -257,14 +257,16 @@ int mhc_device_sm_count(void);
 int mhc_set_path_policy(int policy);
 
 /* 1 if the last mhc_pre_fwd / mhc_head_fwd of the calling thread ran the fused
- * sm_100a kernel, 0 if it ran the generic kernels. */
+ * sm_100a kernel, or its last mhc_pre_bwd / mhc_head_bwd ran the tensor-core
+ * dx / dphi kernel; 0 if it ran the generic kernels. */
 int mhc_last_path(void);
 
 /*
  * First error code recorded by a fused kernel on the current device (0 = none;
- * 1..5 = a bounded wait of the producer / MMA / row / coefficient /
- * pre-aggregate role ran out, which means the kernel gave up instead of
- * hanging and its outputs are invalid).  Synchronises the device.  clear != 0
+ * 1..6 = a bounded wait of the producer / MMA / row / coefficient /
+ * pre-aggregate / Sinkhorn role of the forward kernel ran out, 11..14 = one of
+ * the producer / MMA / epilogue / prep roles of the backward tensor-core
+ * kernel; the kernel gave up instead of hanging and its outputs are invalid).  Synchronises the device.  clear != 0
  * resets the word.  No reference counterpart.
  */
 int mhc_device_error(int clear);

@@ -88,7 +88,10 @@ int mhc_last_path(void) { return g_last_path; }
 
 int mhc_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  return read_tc_error(clear != 0);
+  const int fwd = read_tc_error(clear != 0);
+  const int bwd = read_tcb_error(clear != 0);
+  if (fwd < 0 || bwd < 0) return -1;
+  return fwd != 0 ? fwd : bwd;
 }
 
 size_t mhc_pre_fwd_workspace(int64_t T, int n, int C, int with_res) {
@@ -226,9 +229,11 @@ static int pre_bwd_common(int mode, const void *x, int x_dtype, int64_t T, int n
   if (!workspace || workspace_bytes < plan.total)
     return fail(MHC_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, plan.total);
   if (!aligned(workspace, 256)) return fail(MHC_ERR_ALIGN, "%s: workspace must be 256-byte aligned", who);
+  const bool use_tc = g_policy == MHC_PATH_AUTO && pre_bwd_tc_eligible(mode, n, x_dtype, T, C, x, dz, dx_add, dx);
+  g_last_path = use_tc ? 1 : 0;
   return cuda_status(launch_pre_bwd(mode, n, x_dtype, x, T, C, phi, p, inv_rms, mixes, dz, dh_pre,
                                     dh_post, dh_res, coef_dtype, dx_add, dx, dphi, da_pre, db_pre,
-                                    da_post, db_post, da_res, db_res, workspace, plan,
+                                    da_post, db_post, da_res, db_res, workspace, plan, use_tc,
                                     reinterpret_cast<cudaStream_t>(stream)),
                      who);
 }

@@ -72,7 +72,18 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
                            const void *dx_add, void *dx, void *dphi, void *dalpha_pre,
                            void *dbias_pre, void *dalpha_post, void *dbias_post,
                            void *dalpha_res, void *dbias_res, void *workspace,
-                           const PreBwdPlan &plan, cudaStream_t stream);
+                           const PreBwdPlan &plan, bool use_tc, cudaStream_t stream);
+
+// Tensor-core dx / dphi stage (bf16 x, sm_100a): replaces the CUDA-core one
+// where eligible; `splits` token ranges, one dphi partial each.
+bool pre_bwd_tc_eligible(int mode, int n, int x_dtype, int64_t T, int C, const void *x, const void *dz,
+                         const void *dx_add, const void *dx);
+int pre_bwd_tc_splits(int n, int C, int64_t T, int sm_count, int max_splits);
+cudaError_t launch_pre_bwd_tc(int mode, int n, const void *x, int64_t T, int C, const void *phi, int pdt,
+                              const float *inv_rms, const float *dm, const float *rowb, const float *gate,
+                              const void *dz, const void *dx_add, void *dx, float *dphi_part, int splits,
+                              cudaStream_t stream);
+int read_tcb_error(bool clear);
 
 // ---- stand-alone pieces -----------------------------------------------------
 cudaError_t launch_sinkhorn_fwd(int n, const void *M, int m_dtype, void *Y, int y_dtype,

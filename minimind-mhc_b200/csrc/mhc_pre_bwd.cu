@@ -374,7 +374,7 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
                            const void *dx_add, void *dx, void *dphi, void *dalpha_pre,
                            void *dbias_pre, void *dalpha_post, void *dbias_post,
                            void *dalpha_res, void *dbias_res, void *workspace,
-                           const PreBwdPlan &plan, cudaStream_t stream) {
+                           const PreBwdPlan &plan, bool use_tc, cudaStream_t stream) {
   char *ws = reinterpret_cast<char *>(workspace);
   float *dm_ws = reinterpret_cast<float *>(ws + plan.off_dm);
   float *rowb_ws = reinterpret_cast<float *>(ws + plan.off_rowb);
@@ -383,6 +383,8 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
   float *coef_part = reinterpret_cast<float *>(ws + plan.off_coef_part);
   const int64_t nC = (int64_t)n * C;
   const int sms = device_sm_count();
+  // token splits whose dphi partials K3 sums
+  const int splits = use_tc ? pre_bwd_tc_splits(n, C, T, sms, plan.k2_tsplits) : plan.k2_tsplits;
   return with_mode(mode, [&](auto md) {
     constexpr int MODE = decltype(md)::value;
     return with_n(n, [&](auto nn) {
@@ -408,6 +410,11 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
                                                      vecok);
           if ((e = cudaGetLastError()) != cudaSuccess) return e;
           // K2
+          if (use_tc) {
+            e = launch_pre_bwd_tc(mode, n, x, T, C, phi, p.param_dtype, inv_rms, dm_ws, rowb_ws, gate_ws, dz,
+                                  dx_add, dx, dphi_part, splits, stream);
+            if (e != cudaSuccess) return e;
+          } else {
           constexpr int KC = FD <= 96 ? 64 : 16;
           const size_t smem2 = ((size_t)FD * KC + 32 * (KC + 1) + 32 * FD + 64 + 32 * N) * 4;
           auto k2 = dx_dphi_kernel<N, MODE, Tx>;
@@ -418,13 +425,14 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
                                             rowb_ws, gate_ws, (const Tx *)dz, (const Tx *)dx_add,
                                             (Tx *)dx, dphi_part, plan.k2_tsplits);
           if ((e = cudaGetLastError()) != cudaSuccess) return e;
+          }
         }
         // K3
         const int64_t elems = nC * FD;
         if (dphi) {
           if (T > 0) {
             reduce_dphi_kernel<<<grid_for(elems, 256, sms, 4), 256, 0, stream>>>(
-                dphi_part, plan.k2_tsplits, elems, dphi, p.param_dtype);
+                dphi_part, splits, elems, dphi, p.param_dtype);
           } else {
             reduce_dphi_kernel<<<grid_for(elems, 256, sms, 4), 256, 0, stream>>>(
                 dphi_part, 0, elems, dphi, p.param_dtype);

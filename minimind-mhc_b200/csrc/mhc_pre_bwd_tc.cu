@@ -1,0 +1,535 @@
+// Tensor-core dx / dphi stage of the coefficient backward (sm_100a, bf16 x).
+//
+// Replaces the CUDA-core dx_dphi_kernel for bf16 activations.  After K1 has
+// produced per token dm = dL/dmixes, rowb = inv^2 <dm, m> / nC and the
+// aggregation weights, this kernel computes
+//
+//   dx[t, k]    = inv[t] * (dm[t,:] . phi[k,:]) - rowb[t] x[t,k]
+//                 + w[t, k / C] dz[t, k % C] + dx_add[t, k]
+//   dphi[k, j] += sum_t x[t,k] (inv[t] dm[t,j])
+//
+// One CTA per SM owns 128 consecutive columns k of n*C (inside one stream)
+// and a contiguous range of 128-token tiles.  Both products run on tcgen05
+// with fp32 accumulators in TMEM:
+//
+//   * dx product, M = 128 tokens, N = 128 columns, K = 3*FD (padded to 16):
+//     A = [dm_hi | dm_lo | dm_hi] built per tile by the prep warps, B =
+//     [phi_hi | phi_hi | phi_lo] built once -- three bf16 products give the
+//     fp32 result to ~2^-16.
+//   * dphi product, M = 128 columns, N = 2*FD (padded to 16), K = 128 tokens,
+//     accumulated in TMEM over all tiles of the CTA: A = x^T read straight
+//     from the TMA-staged x tile as an MN-major operand (the tile's 128-byte
+//     rows are tokens, i.e. K), B = [inv*dm hi ; lo] with tokens along K.
+//
+// Warp roles: 0 TMA producer of x tiles (3 stages), 1 MMA issuer, 2-9 the
+// dx epilogue (thread = token row = TMEM lane, two warps per lane quadrant,
+// 64 columns each), 10-13 prep warps (thread = token row).  All hand-offs are
+// mbarriers; every wait is bounded and a timeout sets the device error word.
+// The per-CTA dphi partials go to workspace and are summed in a fixed order
+// by the reduction kernel, so the result is deterministic.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "mhc_device.cuh"
+#include "mhc_dispatch.cuh"
+#include "mhc_kernels.h"
+#include "mhc_sm100.cuh"
+
+namespace mhc {
+
+__device__ int g_tcb_error = 0;  // first error code recorded by the backward tensor-core kernel
+
+namespace tcb {
+
+using namespace sm100;
+
+constexpr int TM = 128;                 // tokens per tile
+constexpr int KCOL = 128;               // columns of n*C per CTA
+constexpr int XS = 3;                   // x tile stages
+constexpr int NEPI = 8, NPREP = 4;
+constexpr int W_PROD = 0, W_MMA = 1, W_EPI = 2, W_PREP = W_EPI + NEPI;
+constexpr int NWARPS = W_PREP + NPREP, NTHREADS = NWARPS * 32;
+constexpr int CHUNK = TM * 128;         // 128 rows x 64 bf16 columns (128-byte swizzle)
+constexpr int XSTAGE = 2 * CHUNK;       // the CTA's 128 columns of one tile
+constexpr int TMEM_COLS = 512;          // D1 x 2 at columns 0 / 128, D2 at 256
+
+enum ErrCode { ERR_PROD = 11, ERR_MMA = 12, ERR_EPI = 13, ERR_PREP = 14 };
+
+template <int N, int MODE>
+struct BCfg {
+  static constexpr int FD = Dims<N, MODE>::FD;
+  static constexpr int K1 = ((3 * FD + 15) / 16) * 16;   // dx product K
+  static constexpr int NB2 = ((2 * FD + 15) / 16) * 16;  // dphi product N
+};
+
+// barrier slots
+constexpr int B_XF = 0, B_XE = XS, B_PF = 2 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
+              B_DRAIN = B_DE + 2, NBARS = B_DRAIN + 1;
+
+struct BLayout {
+  uint32_t xs, b1, a1, b2, bar, tmem, abort, total;
+};
+
+__host__ __device__ inline BLayout make_blayout(int K1, int NB2) {
+  BLayout L;
+  uint32_t o = 0;
+  L.xs = o;    o += XS * XSTAGE;
+  L.b1 = o;    o += (uint32_t)KCOL * K1 * 2;
+  L.a1 = o;    o += 2u * TM * K1 * 2;
+  L.b2 = o;    o += 2u * NB2 * TM * 2;
+  L.bar = o;   o += NBARS * 8;
+  L.tmem = o;  o += 4;
+  L.abort = o; o += 4;
+  L.total = o;
+  return L;
+}
+
+struct BArgs {
+  int64_t T;
+  int C, nC, TS;
+  const void *phi;
+  int pdt;
+  const float *inv_rms, *dm, *rowb, *gate;
+  const __nv_bfloat16 *dz, *dx_add;
+  __nv_bfloat16 *dx;
+  float *dphi_part;  // [TS][nC][FD]
+};
+
+// byte offset of (row r, column k) of a no-swizzle K-major operand built from
+// 8-row x 16-byte core matrices, `kcm` of them per 8-row group along K
+__device__ __forceinline__ uint32_t cm_off(int r, int k, int kcm) {
+  return (uint32_t)(r >> 3) * (uint32_t)(kcm * 128) + (uint32_t)(k >> 3) * 128u + (uint32_t)(r & 7) * 16u +
+         (uint32_t)(k & 7) * 2u;
+}
+
+__device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
+  *abort_flag = 1;
+  atomicCAS(&g_tcb_error, 0, code);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int N, int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1)
+pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
+  using Cf = BCfg<N, MODE>;
+  constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t *base = smem_raw + (base_u32 - raw_u32);
+  const BLayout L = make_blayout(K1, NB2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(base + L.abort);
+  const uint32_t bar0 = base_u32 + L.bar;
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+#define WAIT_WARP(bar, par) (__all_sync(0xffffffffu, wait_parity<false>((bar), (par), abort_flag)))
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nslices = a.nC / KCOL;
+  const int slice = (int)blockIdx.x % nslices, split = (int)blockIdx.x / nslices;
+  const int col0 = slice * KCOL;
+  const int stream_i = col0 / a.C, c_in = col0 - stream_i * a.C;
+  const int64_t tiles = (a.T + TM - 1) / TM;
+  const int64_t tile_beg = tiles * split / a.TS, tile_end = tiles * (split + 1) / a.TS;
+  const int ntile = (int)(tile_end - tile_beg);
+  const int64_t tok_end = tile_end * TM < a.T ? tile_end * TM : a.T;
+
+  // ---------------- prologue ----------------
+  if (tid == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < XS; ++i) {
+      mbar_init(BAR(B_XF + i), 1);
+      mbar_init(BAR(B_XE + i), 1 + NEPI);  // MMA commit + every epilogue warp (they read x too)
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(B_PF + b), NPREP);
+      mbar_init(BAR(B_PE + b), 1);
+      mbar_init(BAR(B_DF + b), 1);
+      mbar_init(BAR(B_DE + b), NEPI);
+    }
+    mbar_init(BAR(B_DRAIN), 1);
+    fence_mbar_init_cluster();
+  }
+  if (warp == W_MMA) {
+    tmem_alloc(base_u32 + L.tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  grid_dep_launch();
+  grid_dep_wait();
+  {
+    // B of the dx product: [phi_hi | phi_hi | phi_lo | 0] for the CTA's columns
+    uint8_t *b1 = base + L.b1;
+    for (int e = tid; e < KCOL * K1; e += NTHREADS) {
+      const int r = e / K1, k = e - r * K1;
+      float v = 0.f;
+      if (k < 3 * FD) {
+        const int j = k < FD ? k : (k < 2 * FD ? k - FD : k - 2 * FD);
+        const float f = load_dyn(a.phi, a.pdt, (int64_t)(col0 + r) * FD + j);
+        const float hi = __bfloat162float(__float2bfloat16_rn(f));
+        v = k < 2 * FD ? hi : f - hi;
+      }
+      *reinterpret_cast<__nv_bfloat16 *>(b1 + cm_off(r, k, K1 / 8)) = __float2bfloat16_rn(v);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
+
+  if (warp == W_PROD) {
+    if (lane == 0) {
+      bool ok = true;
+      int lt = 0;
+      for (; lt < ntile && ok; ++lt) {
+        const int s = lt % XS;
+        if (!wait_parity<false>(BAR(B_XE + s), ((uint32_t)(lt / XS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(BAR(B_XF + s), XSTAGE);
+        const int t0 = (int)((tile_beg + lt) * TM);
+        tma_load_2d(base_u32 + L.xs + s * XSTAGE, &tmap, col0, t0, BAR(B_XF + s));
+        tma_load_2d(base_u32 + L.xs + s * XSTAGE + CHUNK, &tmap, col0 + 64, t0, BAR(B_XF + s));
+      }
+      if (!ok) record_error(ERR_PROD, abort_flag);
+      const int l0 = lt > XS ? lt - XS : 0;
+      for (int p = l0; p < lt; ++p) wait_parity<false>(BAR(B_XF + p % XS), (uint32_t)(p / XS) & 1u, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == W_MMA) {
+    if (lane == 0) {
+      constexpr uint32_t idesc1 = umma_idesc_bf16_f32_major(128, 128, 0, 0);
+      constexpr uint32_t idesc2 = umma_idesc_bf16_f32_major(128, NB2, 1, 0);
+      const uint32_t sbo1 = (uint32_t)(K1 / 8) * 128u;
+      bool ok = true;
+      for (int lt = 0; lt < ntile && ok; ++lt) {
+        const int b = lt & 1, s = lt % XS;
+        const uint32_t bph = (uint32_t)(lt >> 1) & 1u;
+        if (!wait_parity<false>(BAR(B_PF + b), bph, abort_flag)) { ok = false; break; }
+        if (!wait_parity<false>(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u, abort_flag)) { ok = false; break; }
+        if (!wait_parity<false>(BAR(B_DE + b), bph ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        // dx product into D1[b]
+        const uint32_t a1 = base_u32 + L.a1 + (uint32_t)b * TM * K1 * 2;
+        const uint32_t b1 = base_u32 + L.b1;
+#pragma unroll
+        for (int ks = 0; ks < K1 / 16; ++ks)
+          umma_bf16(tmem_base + (uint32_t)b * 128u, umma_desc(a1 + ks * 256, 128, sbo1, 0),
+                    umma_desc(b1 + ks * 256, 128, sbo1, 0), idesc1, ks > 0 ? 1u : 0u);
+        // dphi product, accumulated over every tile: A = x^T (MN-major, the
+        // two 64-column chunks 16 KB apart), B = inv*dm rows, tokens along K
+        const uint32_t xa = base_u32 + L.xs + s * XSTAGE;
+        const uint32_t b2 = base_u32 + L.b2 + (uint32_t)b * NB2 * TM * 2;
+#pragma unroll
+        for (int ks = 0; ks < TM / 16; ++ks)
+          umma_bf16(tmem_base + 256u, umma_desc(xa + ks * 2048, CHUNK, 1024, 2),
+                    umma_desc(b2 + ks * 256, 128, (TM / 8) * 128, 0), idesc2, (lt | ks) != 0 ? 1u : 0u);
+        umma_commit(BAR(B_DF + b));
+        umma_commit(BAR(B_PE + b));
+        umma_commit(BAR(B_XE + s));
+      }
+      if (!ok) record_error(ERR_MMA, abort_flag);
+      umma_commit(BAR(B_DRAIN));
+    }
+    __syncwarp();
+  } else if (warp >= W_PREP) {
+    // ---------------- prep warps: thread = token row of the tile ----------------
+    const int row = tid - W_PREP * 32;
+    bool ok = true;
+    for (int lt = 0; lt < ntile && ok; ++lt) {
+      const int b = lt & 1;
+      if (!WAIT_WARP(BAR(B_PE + b), ((uint32_t)(lt >> 1) & 1u) ^ 1u)) { ok = false; break; }
+      const int64_t tok = (tile_beg + lt) * TM + row;
+      const bool valid = tok < tok_end;
+      float dm[FD];
+      float inv = 0.f;
+#pragma unroll
+      for (int j = 0; j < FD; ++j) dm[j] = 0.f;
+      if (valid) {
+        inv = a.inv_rms[tok];
+        if constexpr (FD % 4 == 0) {
+          const float4 *src = reinterpret_cast<const float4 *>(a.dm + tok * FD);
+#pragma unroll
+          for (int q = 0; q < FD / 4; ++q) {
+            const float4 v = src[q];
+            dm[4 * q] = v.x; dm[4 * q + 1] = v.y; dm[4 * q + 2] = v.z; dm[4 * q + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < FD; ++j) dm[j] = a.dm[tok * FD + j];
+        }
+      }
+      // A of the dx product: row `row` = [dm_hi | dm_lo | dm_hi | 0], 16-byte granules
+      uint8_t *a1 = base + L.a1 + (uint32_t)b * TM * K1 * 2;
+#pragma unroll
+      for (int g = 0; g < K1 / 8; ++g) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int k = g * 8 + e;
+          float val = 0.f;
+          if (k < 3 * FD) {
+            const int j = k < FD ? k : (k < 2 * FD ? k - FD : k - 2 * FD);
+            const float hi = __bfloat162float(__float2bfloat16_rn(dm[j]));
+            val = (k >= FD && k < 2 * FD) ? dm[j] - hi : hi;
+          }
+          v[e] = val;
+        }
+        *reinterpret_cast<uint4 *>(a1 + cm_off(row, g * 8, K1 / 8)) =
+            make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+      }
+      // B of the dphi product: column `row` of [inv*dm hi ; lo ; 0]
+      uint8_t *b2 = base + L.b2 + (uint32_t)b * NB2 * TM * 2;
+#pragma unroll
+      for (int j = 0; j < NB2; ++j) {
+        float val = 0.f;
+        if (j < 2 * FD) {
+          const float di = dm[j < FD ? j : j - FD] * inv;
+          const float hi = __bfloat162float(__float2bfloat16_rn(di));
+          val = j < FD ? hi : di - hi;
+        }
+        *reinterpret_cast<__nv_bfloat16 *>(b2 + cm_off(j, row, TM / 8)) = __float2bfloat16_rn(val);
+      }
+      fence_proxy_async_smem();  // generic writes -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(B_PF + b));
+    }
+    if (!ok) record_error(ERR_PREP, abort_flag);
+  } else {
+    // ---------------- dx epilogue ----------------
+    const int e = warp - W_EPI;
+    const int quad = warp & 3;           // TMEM lane quadrant
+    const int half = e >> 2;             // columns [64*half, 64*half + 64)
+    const int row = quad * 32 + lane;    // token row of the tile = TMEM lane
+    bool ok = true;
+    for (int lt = 0; lt < ntile && ok; ++lt) {
+      const int b = lt & 1, s = lt % XS;
+      const int64_t tok = (tile_beg + lt) * TM + row;
+      const bool valid = tok < tok_end;
+      // independent loads first (dz, dx_add, per-token scalars), then wait for D1
+      uint4 dzv[8], dav[8] = {};
+      float inv = 0.f, rowb = 0.f, wgt = 0.f;
+      if (valid) {
+        const uint4 *dzp = reinterpret_cast<const uint4 *>(a.dz + tok * a.C + c_in + half * 64);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dzv[q] = __ldcs(dzp + q);
+        if (a.dx_add) {
+          const uint4 *dap = reinterpret_cast<const uint4 *>(a.dx_add + tok * a.nC + col0 + half * 64);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) dav[q] = __ldcs(dap + q);
+        }
+        inv = a.inv_rms[tok];
+        rowb = a.rowb[tok];
+        wgt = a.gate[tok * N + stream_i];
+      }
+      if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt >> 1) & 1u)) { ok = false; break; }
+      if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
+      tc_fence_after();
+      const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
+      __nv_bfloat16 *dxp = a.dx + tok * a.nC + col0 + half * 64;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float d1[16];
+        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * 128u + (uint32_t)(half * 64 + g * 16), d1);
+        if (valid) {
+          uint32_t o[8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int q = 2 * g + h;  // 16-byte granule of the 64-column half
+            const uint4 xr = *reinterpret_cast<const uint4 *>(xrow + ((q ^ (row & 7)) << 4));
+            const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
+            const uint32_t zw[4] = {dzv[q].x, dzv[q].y, dzv[q].z, dzv[q].w};
+            const uint32_t aw[4] = {dav[q].x, dav[q].y, dav[q].z, dav[q].w};
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              float xv[2], zv[2], av[2] = {0.f, 0.f};
+              xv[0] = __uint_as_float(xw[p] << 16); xv[1] = __uint_as_float(xw[p] & 0xffff0000u);
+              zv[0] = __uint_as_float(zw[p] << 16); zv[1] = __uint_as_float(zw[p] & 0xffff0000u);
+              if (a.dx_add) { av[0] = __uint_as_float(aw[p] << 16); av[1] = __uint_as_float(aw[p] & 0xffff0000u); }
+              float r[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                float v = inv * d1[h * 8 + 2 * p + u] - rowb * xv[u];
+                v = fmaf(wgt, zv[u], v);
+                r[u] = v + av[u];
+              }
+              o[h * 4 + p] = pack_bf16(r[0], r[1]);
+            }
+          }
+          uint4 *dst = reinterpret_cast<uint4 *>(dxp + g * 16);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(BAR(B_DE + b));
+        mbar_arrive(BAR(B_XE + s));
+      }
+    }
+    if (!ok) record_error(ERR_EPI, abort_flag);
+    // dphi partial of this CTA: D2 lanes are its columns
+    if (half == 0) {
+      const bool drained = WAIT_WARP(BAR(B_DRAIN), 0u);
+      if (drained && ok) {
+        tc_fence_after();
+        float d2[NB2];
+#pragma unroll
+        for (int c16 = 0; c16 < NB2 / 16; ++c16) {
+          float t16[16];
+          tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + 256u + (uint32_t)c16 * 16u, t16);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) d2[c16 * 16 + i] = t16[i];
+        }
+        float *dst = a.dphi_part + ((int64_t)split * a.nC + col0 + row) * FD;
+#pragma unroll
+        for (int j = 0; j < FD; ++j) dst[j] = d2[j] + d2[FD + j];
+      }
+    }
+  }
+
+  // ---------------- teardown ----------------
+  __syncthreads();
+  if (warp == W_MMA) {
+    // every issued MMA has completed before TMEM is released
+    wait_parity<false>(BAR(B_DRAIN), 0u, nullptr);
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+#undef WAIT_WARP
+#undef BAR
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+constexpr size_t SMEM_LIMIT = 232448;
+
+template <int N, int MODE>
+static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t stream) {
+  using Cf = BCfg<N, MODE>;
+  const BLayout L = make_blayout(Cf::K1, Cf::NB2);
+  const size_t smem = (size_t)L.total + 1024;
+  if (smem > SMEM_LIMIT) return cudaErrorNotSupported;
+  auto kern = pre_bwd_tc_kernel<N, MODE>;
+  static std::mutex mu;
+  static size_t smem_set[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem_set[dev & 63] < smem) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      smem_set[dev & 63] = smem;
+    }
+  }
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap tmap;
+  const cuuint64_t dims[2] = {(cuuint64_t)a.nC, (cuuint64_t)a.T};
+  const cuuint64_t strides[1] = {(cuuint64_t)a.nC * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)TM};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorNotSupported;
+  const int nslices = a.nC / KCOL;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)(nslices * a.TS), 1, 1);
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  (void)sms;
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace tcb
+
+int pre_bwd_tc_splits(int n, int C, int64_t T, int sm_count, int max_splits) {
+  const int64_t nC = (int64_t)n * C;
+  const int nslices = (int)(nC / tcb::KCOL);
+  if (nslices <= 0) return 0;
+  int ts = (sm_count > 0 ? sm_count : 148) / nslices;
+  const int64_t tiles = (T + tcb::TM - 1) / tcb::TM;
+  if (ts > tiles) ts = (int)tiles;
+  if (ts > max_splits) ts = max_splits;
+  return ts < 1 ? 1 : ts;
+}
+
+bool pre_bwd_tc_eligible(int mode, int n, int x_dtype, int64_t T, int C, const void *x, const void *dz,
+                         const void *dx_add, const void *dx) {
+  if (x_dtype != MHC_BF16 || T < 1) return false;
+  if (mode == FULL && n > 4) return false;
+  if (n > 8) return false;
+  if (C % tcb::KCOL != 0) return false;  // a CTA's 128 columns lie inside one stream
+  const uintptr_t m = (uintptr_t)x | (uintptr_t)dz | (uintptr_t)dx | (uintptr_t)dx_add;
+  if ((m & 15) != 0) return false;
+  return true;
+}
+
+cudaError_t launch_pre_bwd_tc(int mode, int n, const void *x, int64_t T, int C, const void *phi, int pdt,
+                              const float *inv_rms, const float *dm, const float *rowb, const float *gate,
+                              const void *dz, const void *dx_add, void *dx, float *dphi_part, int splits,
+                              cudaStream_t stream) {
+  tcb::BArgs a;
+  a.T = T;
+  a.C = C;
+  a.nC = n * C;
+  a.TS = splits;
+  a.phi = phi;
+  a.pdt = pdt;
+  a.inv_rms = inv_rms;
+  a.dm = dm;
+  a.rowb = rowb;
+  a.gate = gate;
+  a.dz = reinterpret_cast<const __nv_bfloat16 *>(dz);
+  a.dx_add = reinterpret_cast<const __nv_bfloat16 *>(dx_add);
+  a.dx = reinterpret_cast<__nv_bfloat16 *>(dx);
+  a.dphi_part = dphi_part;
+  const int sms = device_sm_count();
+  return with_mode(mode, [&](auto md) -> cudaError_t {
+    constexpr int MODE = decltype(md)::value;
+    switch (n) {
+      case 1: return tcb::launch_impl<1, MODE>(x, a, sms, stream);
+      case 2: return tcb::launch_impl<2, MODE>(x, a, sms, stream);
+      case 4: return tcb::launch_impl<4, MODE>(x, a, sms, stream);
+      case 8: if constexpr (MODE != FULL) return tcb::launch_impl<8, MODE>(x, a, sms, stream); break;
+      default: break;
+    }
+    return cudaErrorNotSupported;
+  });
+}
+
+int read_tcb_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tcb_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_tcb_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace mhc
