@@ -21,9 +21,10 @@
 //     from the TMA-staged x tile as an MN-major operand (the tile's 128-byte
 //     rows are tokens, i.e. K), B = [inv*dm hi ; lo] with tokens along K.
 //
-// Warp roles: 0 TMA producer of x tiles (3 stages), 1 MMA issuer, 2-9 the
-// dx epilogue (thread = token row = TMEM lane, two warps per lane quadrant,
-// 64 columns each), 10-13 prep warps (thread = token row).  All hand-offs are
+// Warp roles: 0 TMA producer of the x and dx_add tiles (2 stages), 1 MMA
+// issuer, 2-9 the dx epilogue (thread = token row = TMEM lane, two warps per
+// lane quadrant, 64 columns each; dz is loaded one tile ahead), 10-13 prep
+// warps (thread = token row).  All hand-offs are
 // mbarriers; every wait is bounded and a timeout sets the device error word.
 // The per-CTA dphi partials go to workspace and are summed in a fixed order
 // by the reduction kernel, so the result is deterministic.
@@ -47,12 +48,12 @@ using namespace sm100;
 
 constexpr int TM = 128;                 // tokens per tile
 constexpr int KCOL = 128;               // columns of n*C per CTA
-constexpr int XS = 3;                   // x tile stages
+constexpr int XS = 2;                   // tile stages (x and dx_add)
 constexpr int NEPI = 8, NPREP = 4;
 constexpr int W_PROD = 0, W_MMA = 1, W_EPI = 2, W_PREP = W_EPI + NEPI;
 constexpr int NWARPS = W_PREP + NPREP, NTHREADS = NWARPS * 32;
 constexpr int CHUNK = TM * 128;         // 128 rows x 64 bf16 columns (128-byte swizzle)
-constexpr int XSTAGE = 2 * CHUNK;       // the CTA's 128 columns of one tile
+constexpr int XSTAGE = 4 * CHUNK;       // x then dx_add, the CTA's 128 columns of one tile each
 constexpr int TMEM_COLS = 512;          // D1 x 2 at columns 0 / 128, D2 at 256
 
 enum ErrCode { ERR_PROD = 11, ERR_MMA = 12, ERR_EPI = 13, ERR_PREP = 14 };
@@ -116,7 +117,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 template <int N, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
+pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap amap, BArgs a) {
   using Cf = BCfg<N, MODE>;
   constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2;
   extern __shared__ uint8_t smem_raw[];
@@ -187,10 +188,14 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
       for (; lt < ntile && ok; ++lt) {
         const int s = lt % XS;
         if (!wait_parity<false>(BAR(B_XE + s), ((uint32_t)(lt / XS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(BAR(B_XF + s), XSTAGE);
+        mbar_arrive_expect_tx(BAR(B_XF + s), a.dx_add ? XSTAGE : 2 * CHUNK);
         const int t0 = (int)((tile_beg + lt) * TM);
         tma_load_2d(base_u32 + L.xs + s * XSTAGE, &tmap, col0, t0, BAR(B_XF + s));
         tma_load_2d(base_u32 + L.xs + s * XSTAGE + CHUNK, &tmap, col0 + 64, t0, BAR(B_XF + s));
+        if (a.dx_add) {
+          tma_load_2d(base_u32 + L.xs + s * XSTAGE + 2 * CHUNK, &amap, col0, t0, BAR(B_XF + s));
+          tma_load_2d(base_u32 + L.xs + s * XSTAGE + 3 * CHUNK, &amap, col0 + 64, t0, BAR(B_XF + s));
+        }
       }
       if (!ok) record_error(ERR_PROD, abort_flag);
       const int l0 = lt > XS ? lt - XS : 0;
@@ -303,30 +308,34 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
     const int half = e >> 2;             // columns [64*half, 64*half + 64)
     const int row = quad * 32 + lane;    // token row of the tile = TMEM lane
     bool ok = true;
+    // dz rows of the next tile are loaded while the current tile is finished
+    uint4 dzv[8];
+    auto load_dz = [&](int lt_, uint4 (&dst)[8]) {
+      const int64_t tk = (tile_beg + lt_) * TM + row;
+      if (lt_ < ntile && tk < tok_end) {
+        const uint4 *dzp = reinterpret_cast<const uint4 *>(a.dz + tk * a.C + c_in + half * 64);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = __ldcs(dzp + q);
+      }
+    };
+    load_dz(0, dzv);
     for (int lt = 0; lt < ntile && ok; ++lt) {
       const int b = lt & 1, s = lt % XS;
       const int64_t tok = (tile_beg + lt) * TM + row;
       const bool valid = tok < tok_end;
-      // independent loads first (dz, dx_add, per-token scalars), then wait for D1
-      uint4 dzv[8], dav[8] = {};
       float inv = 0.f, rowb = 0.f, wgt = 0.f;
       if (valid) {
-        const uint4 *dzp = reinterpret_cast<const uint4 *>(a.dz + tok * a.C + c_in + half * 64);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) dzv[q] = __ldcs(dzp + q);
-        if (a.dx_add) {
-          const uint4 *dap = reinterpret_cast<const uint4 *>(a.dx_add + tok * a.nC + col0 + half * 64);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) dav[q] = __ldcs(dap + q);
-        }
         inv = a.inv_rms[tok];
         rowb = a.rowb[tok];
         wgt = a.gate[tok * N + stream_i];
       }
+      uint4 dzn[8];
+      load_dz(lt + 1, dzn);
       if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt >> 1) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
+      const uint8_t *arow = xrow + 2 * CHUNK;  // dx_add tile, same layout
       __nv_bfloat16 *dxp = a.dx + tok * a.nC + col0 + half * 64;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
@@ -337,16 +346,18 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int q = 2 * g + h;  // 16-byte granule of the 64-column half
-            const uint4 xr = *reinterpret_cast<const uint4 *>(xrow + ((q ^ (row & 7)) << 4));
+            const uint32_t goff = (uint32_t)((q ^ (row & 7)) << 4);
+            const uint4 xr = *reinterpret_cast<const uint4 *>(xrow + goff);
+            uint4 ar = make_uint4(0u, 0u, 0u, 0u);
+            if (a.dx_add) ar = *reinterpret_cast<const uint4 *>(arow + goff);
             const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
             const uint32_t zw[4] = {dzv[q].x, dzv[q].y, dzv[q].z, dzv[q].w};
-            const uint32_t aw[4] = {dav[q].x, dav[q].y, dav[q].z, dav[q].w};
+            const uint32_t aw[4] = {ar.x, ar.y, ar.z, ar.w};
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
-              float xv[2], zv[2], av[2] = {0.f, 0.f};
-              xv[0] = __uint_as_float(xw[p] << 16); xv[1] = __uint_as_float(xw[p] & 0xffff0000u);
-              zv[0] = __uint_as_float(zw[p] << 16); zv[1] = __uint_as_float(zw[p] & 0xffff0000u);
-              if (a.dx_add) { av[0] = __uint_as_float(aw[p] << 16); av[1] = __uint_as_float(aw[p] & 0xffff0000u); }
+              const float xv[2] = {__uint_as_float(xw[p] << 16), __uint_as_float(xw[p] & 0xffff0000u)};
+              const float zv[2] = {__uint_as_float(zw[p] << 16), __uint_as_float(zw[p] & 0xffff0000u)};
+              const float av[2] = {__uint_as_float(aw[p] << 16), __uint_as_float(aw[p] & 0xffff0000u)};
               float r[2];
 #pragma unroll
               for (int u = 0; u < 2; ++u) {
@@ -368,6 +379,8 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, BArgs a) {
         mbar_arrive(BAR(B_DE + b));
         mbar_arrive(BAR(B_XE + s));
       }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
     }
     if (!ok) record_error(ERR_EPI, abort_flag);
     // dphi partial of this CTA: D2 lanes are its columns
@@ -439,15 +452,19 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   }
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  CUtensorMap tmap;
+  // x and dx_add as (T rows) x (nC columns): 128-row x 64-column boxes, 128-byte swizzle
+  CUtensorMap tmap, amap;
   const cuuint64_t dims[2] = {(cuuint64_t)a.nC, (cuuint64_t)a.T};
   const cuuint64_t strides[1] = {(cuuint64_t)a.nC * 2};
   const cuuint32_t box[2] = {64, (cuuint32_t)TM};
   const cuuint32_t estr[2] = {1, 1};
-  if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorNotSupported;
+  const void *srcs[2] = {x, a.dx_add ? (const void *)a.dx_add : x};
+  CUtensorMap *maps[2] = {&tmap, &amap};
+  for (int m = 0; m < 2; ++m)
+    if (enc(maps[m], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(srcs[m]), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorNotSupported;
   const int nslices = a.nC / KCOL;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -460,7 +477,7 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   (void)sms;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, a);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, amap, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
