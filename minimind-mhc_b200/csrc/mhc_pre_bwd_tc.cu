@@ -66,8 +66,12 @@ struct BCfg {
 };
 
 // barrier slots
-constexpr int B_XF = 0, B_XE = XS, B_PF = 2 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
+constexpr int B_XF = 0, B_XE = XS, B_SR = 2 * XS, B_PF = 3 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
               B_DRAIN = B_DE + 2, NBARS = B_DRAIN + 1;
+
+// A of the dx product: 8-row groups are padded by one 16-byte granule so the
+// prep threads' row writes do not collide on shared-memory banks
+__host__ __device__ constexpr uint32_t a1_sbo(int K1) { return (uint32_t)(K1 / 8) * 128u + 16u; }
 
 struct BLayout {
   uint32_t xs, b1, a1, b2, bar, tmem, abort, total;
@@ -78,7 +82,7 @@ __host__ __device__ inline BLayout make_blayout(int K1, int NB2) {
   uint32_t o = 0;
   L.xs = o;    o += XS * XSTAGE;
   L.b1 = o;    o += (uint32_t)KCOL * K1 * 2;
-  L.a1 = o;    o += 2u * TM * K1 * 2;
+  L.a1 = o;    o += 2u * (TM / 8) * a1_sbo(K1);
   L.b2 = o;    o += 2u * NB2 * TM * 2;
   L.bar = o;   o += NBARS * 8;
   L.tmem = o;  o += 4;
@@ -99,10 +103,16 @@ struct BArgs {
 };
 
 // byte offset of (row r, column k) of a no-swizzle K-major operand built from
-// 8-row x 16-byte core matrices, `kcm` of them per 8-row group along K
-__device__ __forceinline__ uint32_t cm_off(int r, int k, int kcm) {
-  return (uint32_t)(r >> 3) * (uint32_t)(kcm * 128) + (uint32_t)(k >> 3) * 128u + (uint32_t)(r & 7) * 16u +
-         (uint32_t)(k & 7) * 2u;
+// 8-row x 16-byte core matrices (8-row groups `sbo` bytes apart, the core
+// matrices of a group contiguous along K)
+__device__ __forceinline__ uint32_t cm_off(int r, int k, uint32_t sbo) {
+  return (uint32_t)(r >> 3) * sbo + (uint32_t)(k >> 3) * 128u + (uint32_t)(r & 7) * 16u + (uint32_t)(k & 7) * 2u;
+}
+// byte offset of (MN index n, K index k) of a no-swizzle MN-major operand:
+// one 16-byte granule holds 8 consecutive n of one k; the 8 k of a group are
+// consecutive granules (K groups 128 B apart), MN blocks of 8 `sbo` bytes apart
+__device__ __forceinline__ uint32_t mn_off(int n, int k, uint32_t sbo) {
+  return (uint32_t)(n >> 3) * sbo + (uint32_t)(k >> 3) * 128u + (uint32_t)(k & 7) * 16u + (uint32_t)(n & 7) * 2u;
 }
 
 __device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
@@ -117,7 +127,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 template <int N, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
-pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap amap, BArgs a) {
+pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap amap,
+                  const __grid_constant__ CUtensorMap dmap, BArgs a) {
   using Cf = BCfg<N, MODE>;
   constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2;
   extern __shared__ uint8_t smem_raw[];
@@ -145,7 +156,8 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     *abort_flag = 0;
     for (int i = 0; i < XS; ++i) {
       mbar_init(BAR(B_XF + i), 1);
-      mbar_init(BAR(B_XE + i), 1 + NEPI);  // MMA commit + every epilogue warp (they read x too)
+      mbar_init(BAR(B_XE + i), 2);         // MMA commit + the dx store has read the stage
+      mbar_init(BAR(B_SR + i), NEPI);      // every epilogue warp wrote its dx part into the stage
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(B_PF + b), NPREP);
@@ -174,7 +186,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         const float hi = __bfloat162float(__float2bfloat16_rn(f));
         v = k < 2 * FD ? hi : f - hi;
       }
-      *reinterpret_cast<__nv_bfloat16 *>(b1 + cm_off(r, k, K1 / 8)) = __float2bfloat16_rn(v);
+      *reinterpret_cast<__nv_bfloat16 *>(b1 + cm_off(r, k, (K1 / 8) * 128u)) = __float2bfloat16_rn(v);
     }
   }
   fence_proxy_async_smem();
@@ -205,7 +217,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
   } else if (warp == W_MMA) {
     if (lane == 0) {
       constexpr uint32_t idesc1 = umma_idesc_bf16_f32_major(128, 128, 0, 0);
-      constexpr uint32_t idesc2 = umma_idesc_bf16_f32_major(128, NB2, 1, 0);
+      constexpr uint32_t idesc2 = umma_idesc_bf16_f32_major(128, NB2, 1, 1);
       const uint32_t sbo1 = (uint32_t)(K1 / 8) * 128u;
       bool ok = true;
       for (int lt = 0; lt < ntile && ok; ++lt) {
@@ -216,20 +228,21 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         if (!wait_parity<false>(BAR(B_DE + b), bph ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         // dx product into D1[b]
-        const uint32_t a1 = base_u32 + L.a1 + (uint32_t)b * TM * K1 * 2;
+        const uint32_t a1 = base_u32 + L.a1 + (uint32_t)b * (TM / 8) * a1_sbo(K1);
         const uint32_t b1 = base_u32 + L.b1;
 #pragma unroll
         for (int ks = 0; ks < K1 / 16; ++ks)
-          umma_bf16(tmem_base + (uint32_t)b * 128u, umma_desc(a1 + ks * 256, 128, sbo1, 0),
+          umma_bf16(tmem_base + (uint32_t)b * 128u, umma_desc(a1 + ks * 256, 128, a1_sbo(K1), 0),
                     umma_desc(b1 + ks * 256, 128, sbo1, 0), idesc1, ks > 0 ? 1u : 0u);
         // dphi product, accumulated over every tile: A = x^T (MN-major, the
-        // two 64-column chunks 16 KB apart), B = inv*dm rows, tokens along K
+        // two 64-column chunks 16 KB apart), B = inv*dm (MN-major, 8-feature
+        // blocks TM*16 bytes apart), tokens along K for both
         const uint32_t xa = base_u32 + L.xs + s * XSTAGE;
         const uint32_t b2 = base_u32 + L.b2 + (uint32_t)b * NB2 * TM * 2;
 #pragma unroll
         for (int ks = 0; ks < TM / 16; ++ks)
           umma_bf16(tmem_base + 256u, umma_desc(xa + ks * 2048, CHUNK, 1024, 2),
-                    umma_desc(b2 + ks * 256, 128, (TM / 8) * 128, 0), idesc2, (lt | ks) != 0 ? 1u : 0u);
+                    umma_desc(b2 + ks * 256, 128, TM * 16, 0), idesc2, (lt | ks) != 0 ? 1u : 0u);
         umma_commit(BAR(B_DF + b));
         umma_commit(BAR(B_PE + b));
         umma_commit(BAR(B_XE + s));
@@ -266,7 +279,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         }
       }
       // A of the dx product: row `row` = [dm_hi | dm_lo | dm_hi | 0], 16-byte granules
-      uint8_t *a1 = base + L.a1 + (uint32_t)b * TM * K1 * 2;
+      uint8_t *a1 = base + L.a1 + (uint32_t)b * (TM / 8) * a1_sbo(K1);
 #pragma unroll
       for (int g = 0; g < K1 / 8; ++g) {
         float v[8];
@@ -281,20 +294,28 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
           }
           v[e] = val;
         }
-        *reinterpret_cast<uint4 *>(a1 + cm_off(row, g * 8, K1 / 8)) =
+        *reinterpret_cast<uint4 *>(a1 + cm_off(row, g * 8, a1_sbo(K1))) =
             make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
       }
-      // B of the dphi product: column `row` of [inv*dm hi ; lo ; 0]
+      // B of the dphi product (MN-major): token `row` holds [inv*dm hi | lo | 0],
+      // written as 16-byte granules of 8 features
       uint8_t *b2 = base + L.b2 + (uint32_t)b * NB2 * TM * 2;
 #pragma unroll
-      for (int j = 0; j < NB2; ++j) {
-        float val = 0.f;
-        if (j < 2 * FD) {
-          const float di = dm[j < FD ? j : j - FD] * inv;
-          const float hi = __bfloat162float(__float2bfloat16_rn(di));
-          val = j < FD ? hi : di - hi;
+      for (int g = 0; g < NB2 / 8; ++g) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int j = g * 8 + e;
+          float val = 0.f;
+          if (j < 2 * FD) {
+            const float di = dm[j < FD ? j : j - FD] * inv;
+            const float hi = __bfloat162float(__float2bfloat16_rn(di));
+            val = j < FD ? hi : di - hi;
+          }
+          v[e] = val;
         }
-        *reinterpret_cast<__nv_bfloat16 *>(b2 + cm_off(j, row, TM / 8)) = __float2bfloat16_rn(val);
+        *reinterpret_cast<uint4 *>(b2 + mn_off(g * 8, row, TM * 16)) =
+            make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
       }
       fence_proxy_async_smem();  // generic writes -> tensor-core reads
       __syncwarp();
@@ -335,8 +356,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
-      const uint8_t *arow = xrow + 2 * CHUNK;  // dx_add tile, same layout
-      __nv_bfloat16 *dxp = a.dx + tok * a.nC + col0 + half * 64;
+      uint8_t *arow = base + L.xs + s * XSTAGE + (2 + half) * CHUNK + row * 128;  // dx_add tile; dx goes back here
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         float d1[16];
@@ -367,22 +387,40 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
               }
               o[h * 4 + p] = pack_bf16(r[0], r[1]);
             }
+            // dx replaces the dx_add granule it was computed from (same thread)
+            *reinterpret_cast<uint4 *>(arow + goff) = make_uint4(o[h * 4], o[h * 4 + 1], o[h * 4 + 2], o[h * 4 + 3]);
           }
-          uint4 *dst = reinterpret_cast<uint4 *>(dxp + g * 16);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
       }
       tc_fence_before();
+      fence_proxy_async_smem();  // dx written through the generic proxy, read by the TMA store
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(BAR(B_DE + b));
-        mbar_arrive(BAR(B_XE + s));
+        mbar_arrive(BAR(B_SR + s));
+      }
+      // one thread stores the tile's dx with two TMA boxes (rows past T are
+      // clipped by the tensor map), then frees the stage once they are read
+      if (warp == W_EPI) {
+        int good = 1;
+        if (lane == 0) {
+          good = wait_parity<false>(BAR(B_SR + s), (uint32_t)(lt / XS) & 1u, abort_flag) ? 1 : 0;
+          if (good) {
+            const int t0 = (int)((tile_beg + lt) * TM);
+            tma_store_2d(&dmap, base_u32 + L.xs + s * XSTAGE + 2 * CHUNK, col0, t0);
+            tma_store_2d(&dmap, base_u32 + L.xs + s * XSTAGE + 3 * CHUNK, col0 + 64, t0);
+            bulk_commit();
+            bulk_wait_read0();
+            mbar_arrive(BAR(B_XE + s));
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
     }
     if (!ok) record_error(ERR_EPI, abort_flag);
+    if (warp == W_EPI && lane == 0) bulk_wait0();  // every dx store has completed
     // dphi partial of this CTA: D2 lanes are its columns
     if (half == 0) {
       const bool drained = WAIT_WARP(BAR(B_DRAIN), 0u);
@@ -453,14 +491,14 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   // x and dx_add as (T rows) x (nC columns): 128-row x 64-column boxes, 128-byte swizzle
-  CUtensorMap tmap, amap;
+  CUtensorMap tmap, amap, dmap;
   const cuuint64_t dims[2] = {(cuuint64_t)a.nC, (cuuint64_t)a.T};
   const cuuint64_t strides[1] = {(cuuint64_t)a.nC * 2};
   const cuuint32_t box[2] = {64, (cuuint32_t)TM};
   const cuuint32_t estr[2] = {1, 1};
-  const void *srcs[2] = {x, a.dx_add ? (const void *)a.dx_add : x};
-  CUtensorMap *maps[2] = {&tmap, &amap};
-  for (int m = 0; m < 2; ++m)
+  const void *srcs[3] = {x, a.dx_add ? (const void *)a.dx_add : x, a.dx};
+  CUtensorMap *maps[3] = {&tmap, &amap, &dmap};
+  for (int m = 0; m < 3; ++m)
     if (enc(maps[m], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(srcs[m]), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -477,7 +515,7 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   (void)sms;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, amap, a);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, amap, dmap, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
