@@ -57,6 +57,8 @@ CASES = [
     (2, 512, 300, True),
     (4, 512, 777, True),
     (8, 512, 260, False),
+    (2, 768, 515, False),
+    (4, 768, 16 * 128 * 15 + 3, True),  # every cluster busy, a partial last tile
 ]
 
 
