@@ -60,7 +60,7 @@ struct PreBwdPlan {
   int k2_kc;         // k columns per block of the dx / dphi kernel
   int k2_kblocks;    // ceil(nC / kc)
   int k2_tsplits;    // token splits (one dphi partial per split)
-  size_t off_dm, off_rowb, off_gate, off_dphi_part, off_coef_part, total;
+  size_t off_dm, off_rowb, off_gate, off_dphi_part, off_coef_part, off_dots, total;
 };
 
 PreBwdPlan plan_pre_bwd(int mode, int n, int64_t T, int C, int sk_iters, int sm_count);

@@ -1,11 +1,15 @@
 // Backward of the coefficient stage + pre-aggregate (generic CUDA-core path).
 //
-// Three launches, no atomics (deterministic):
-//  K1 coef_bwd_kernel  : per token, the dot products <dz, x_i> (one warp per
-//     token), then one thread per token runs the gate / Sinkhorn backward (the
-//     Sinkhorn trajectory is recomputed into shared memory) and writes dm =
-//     dL/dmixes, the RMS-backward row coefficient and the aggregation weights.
-//     Per-block sums of the alpha / bias gradients go to the workspace.
+// Launches, no atomics (deterministic):
+//  K1a coef_dots_kernel: per token, the dot products <dz, x_i>: a streaming
+//     pass over x and dz, one warp per token with every load of a round in
+//     flight before the first FMA.
+//  K1 coef_bwd_kernel  : one thread per token runs the gate / Sinkhorn
+//     backward (the Sinkhorn trajectory is recomputed into shared memory) and
+//     writes dm = dL/dmixes, the RMS-backward row coefficient and the
+//     aggregation weights.  Per-block sums of the alpha / bias gradients go to
+//     the workspace.  (Without K1a's dots it computes them itself, one warp per
+//     token.)
 //  K2 dx_dphi_kernel   : grid (k-chunks x token splits).  For its k-chunk a block
 //     keeps phi^T in shared memory and, per 32-token tile,
 //       dx = inv*(dm @ phi^T) - rowb*x + w_i*dz + dx_add
@@ -59,8 +63,80 @@ PreBwdPlan plan_pre_bwd(int mode, int n, int64_t T, int C, int sk_iters, int sm_
   p.off_gate = off;      off = align256(off + (size_t)T * n * 4);
   p.off_dphi_part = off; off = align256(off + (size_t)p.k2_tsplits * nC * p.fd * 4);
   p.off_coef_part = off; off = align256(off + (size_t)(p.k1_blocks > 0 ? p.k1_blocks : 1) * ng_of(mode, n) * 4);
+  p.off_dots = off;      off = align256(off + (size_t)T * n * 4);
   p.total = off;
   return p;
+}
+
+// ---------------------------------------------------------------------------
+// K1a
+// ---------------------------------------------------------------------------
+// dots[t, i] = <dz[t, :], x[t, i*C : (i+1)*C]>.  One warp per token; a round
+// takes U 16-byte vectors per lane of dz and of every stream (5 U loads in
+// flight per lane at n = 4) before any FMA.  x streams through L2 (evict
+// first); dz keeps the default policy, the dx kernel reads it again.
+template <int N, typename Tx>
+__global__ void __launch_bounds__(256)
+coef_dots_kernel(const Tx *__restrict__ x, const Tx *__restrict__ dz, int64_t T, int C,
+                 float *__restrict__ dots, bool vecok) {
+  constexpr int VEC = 16 / sizeof(Tx);
+  constexpr int U = N <= 4 ? 3 : 1;  // rounds of loads stay within ~64 registers
+  const int lane = threadIdx.x & 31;
+  const int64_t wg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t nC = (int64_t)N * C;
+  for (int64_t tok = wg; tok < T; tok += nw) {
+    float d[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = 0.f;
+    const Tx *xr = x + tok * nC;
+    const Tx *gr = dz + tok * C;
+    if (vecok) {
+      const int vpt = C / VEC;
+      for (int v0 = lane; v0 < vpt; v0 += 32 * U) {
+        uint4 g[U], xv[N][U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int v = v0 + u * 32;
+          if (v < vpt) {
+            g[u] = ldg_keep(gr + (int64_t)v * VEC);
+#pragma unroll
+            for (int i = 0; i < N; ++i) xv[i][u] = ldg_stream(xr + (int64_t)i * C + (int64_t)v * VEC);
+          } else {
+            g[u] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int i = 0; i < N; ++i) xv[i][u] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          Pack<Tx> pg;
+          pg.raw = g[u];
+          float gf[VEC];
+          pg.to_float(gf);
+#pragma unroll
+          for (int i = 0; i < N; ++i) {
+            Pack<Tx> px;
+            px.raw = xv[i][u];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) d[i] = fmaf(gf[e], px.get(e), d[i]);
+          }
+        }
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) {
+        const float g = to_f(gr[c]);
+#pragma unroll
+        for (int i = 0; i < N; ++i) d[i] = fmaf(g, to_f(xr[(int64_t)i * C + c]), d[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = warp_sum(d[i]);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) dots[tok * N + i] = d[i];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -73,7 +149,7 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
                 const Tx *__restrict__ dz, const void *dh_pre, const void *dh_post,
                 const void *dh_res, int coef_dtype, int TB,
                 float *__restrict__ dm_ws, float *__restrict__ rowb_ws, float *__restrict__ gate_ws,
-                float *__restrict__ coef_part, bool vecok) {
+                float *__restrict__ coef_part, bool vecok, const float *__restrict__ dots_in) {
   constexpr int FD = Dims<N, MODE>::FD;
   constexpr int NG = 3 + FD;
   constexpr int NPAR = 3 + 2 * N + N * N;
@@ -100,9 +176,9 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
     par[i] = v;
   }
 
-  // phase 1: <dz, x_i> per token, one warp per token
+  // phase 1: <dz, x_i> per token, one warp per token (unless K1a made them)
   const int vpt = vecok ? C / VEC : C;
-  for (int t = warp; t < TB; t += (blockDim.x >> 5)) {
+  for (int t = warp; !dots_in && t < TB; t += (blockDim.x >> 5)) {
     const int64_t tok = tok0 + t;
     float d[N];
 #pragma unroll
@@ -158,7 +234,7 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
       for (int i = 0; i < N; ++i) {
         const float s = sigmoidf_(__fadd_rn(__fmul_rn(m[i], par[0]), par[3 + i]));
         gate_ws[tok * N + i] = s + p.pre_eps;
-        const float da = dots[t * N + i] * s * (1.f - s);
+        const float da = (dots_in ? dots_in[tok * N + i] : dots[t * N + i]) * s * (1.f - s);
         dm[i] = par[0] * da;
         g_out[0] += da * m[i];
         g_out[3 + i] = da;
@@ -168,7 +244,7 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
       for (int i = 0; i < N; ++i) {
         const float sp = sigmoidf_(__fadd_rn(__fmul_rn(m[i], par[0]), par[3 + i]));
         gate_ws[tok * N + i] = sp + p.pre_eps;
-        float gp = dots[t * N + i];
+        float gp = dots_in ? dots_in[tok * N + i] : dots[t * N + i];
         if (dh_pre) gp += load_dyn(dh_pre, coef_dtype, tok * N + i);
         const float dpre = gp * sp * (1.f - sp);
         dm[i] = par[0] * dpre;
@@ -401,13 +477,22 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
           const size_t traj = (MODE == FULL && p.apply_sinkhorn) ? (size_t)steps * N * N * TB : 0;
           const size_t smem1 = ((size_t)(3 + 2 * N + N * N) + (size_t)TB * N + (size_t)TB * NG + traj) * 4;
           const bool vecok = C % VEC == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)dz & 15) == 0;
-          auto k1 = coef_bwd_kernel<N, MODE, Tx>;
-          cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+          // K1a: the dot products, a streaming pass with every SM busy
+          float *dots = reinterpret_cast<float *>(ws + plan.off_dots);
+          const int64_t dblocks_need = (T + 7) / 8;
+          const int64_t dblocks_cap = (int64_t)(sms > 0 ? sms : 148) * 16;
+          coef_dots_kernel<N, Tx><<<(unsigned)(dblocks_need < dblocks_cap ? dblocks_need : dblocks_cap), 256, 0,
+                                    stream>>>((const Tx *)x, (const Tx *)dz, T, C, dots, vecok);
+          cudaError_t e = cudaGetLastError();
           if (e != cudaSuccess) return e;
-          k1<<<plan.k1_blocks, 256, smem1, stream>>>((const Tx *)x, T, C, p, inv_rms, mixes,
-                                                     (const Tx *)dz, dh_pre, dh_post, dh_res,
-                                                     coef_dtype, TB, dm_ws, rowb_ws, gate_ws, coef_part,
-                                                     vecok);
+          // K1: one thread per token (TB tokens per block, one warp)
+          auto k1 = coef_bwd_kernel<N, MODE, Tx>;
+          e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+          if (e != cudaSuccess) return e;
+          k1<<<plan.k1_blocks, 32, smem1, stream>>>((const Tx *)x, T, C, p, inv_rms, mixes,
+                                                    (const Tx *)dz, dh_pre, dh_post, dh_res,
+                                                    coef_dtype, TB, dm_ws, rowb_ws, gate_ws, coef_part,
+                                                    vecok, dots);
           if ((e = cudaGetLastError()) != cudaSuccess) return e;
           // K2
           if (use_tc) {

@@ -329,29 +329,29 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     const int half = e >> 2;             // columns [64*half, 64*half + 64)
     const int row = quad * 32 + lane;    // token row of the tile = TMEM lane
     bool ok = true;
-    // dz rows of the next tile are loaded while the current tile is finished
+    // dz row and per-token scalars of the next tile are loaded while the
+    // current tile is finished
     uint4 dzv[8];
-    auto load_dz = [&](int lt_, uint4 (&dst)[8]) {
+    float inv = 0.f, rowb = 0.f, wgt = 0.f;
+    auto load_next = [&](int lt_, uint4 (&dst)[8], float &inv_, float &rowb_, float &wgt_) {
       const int64_t tk = (tile_beg + lt_) * TM + row;
       if (lt_ < ntile && tk < tok_end) {
         const uint4 *dzp = reinterpret_cast<const uint4 *>(a.dz + tk * a.C + c_in + half * 64);
 #pragma unroll
         for (int q = 0; q < 8; ++q) dst[q] = __ldcs(dzp + q);
+        inv_ = a.inv_rms[tk];
+        rowb_ = a.rowb[tk];
+        wgt_ = a.gate[tk * N + stream_i];
       }
     };
-    load_dz(0, dzv);
+    load_next(0, dzv, inv, rowb, wgt);
     for (int lt = 0; lt < ntile && ok; ++lt) {
       const int b = lt & 1, s = lt % XS;
       const int64_t tok = (tile_beg + lt) * TM + row;
       const bool valid = tok < tok_end;
-      float inv = 0.f, rowb = 0.f, wgt = 0.f;
-      if (valid) {
-        inv = a.inv_rms[tok];
-        rowb = a.rowb[tok];
-        wgt = a.gate[tok * N + stream_i];
-      }
       uint4 dzn[8];
-      load_dz(lt + 1, dzn);
+      float inv_n = 0.f, rowb_n = 0.f, wgt_n = 0.f;
+      load_next(lt + 1, dzn, inv_n, rowb_n, wgt_n);
       if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt >> 1) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
       tc_fence_after();
@@ -418,6 +418,9 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
+      inv = inv_n;
+      rowb = rowb_n;
+      wgt = wgt_n;
     }
     if (!ok) record_error(ERR_EPI, abort_flag);
     if (warp == W_EPI && lane == 0) bulk_wait0();  // every dx store has completed
