@@ -255,56 +255,92 @@ MHC_UNROLL_N
   }
 }
 
-// Sinkhorn backward by recompute.  `traj` is caller scratch with room for
-// max(iters,1) matrices of N*N floats at stride `tstride` floats between
-// consecutive matrices (so a block can interleave threads); on entry `m` holds
-// the logits, `g` the gradient w.r.t. the output; on exit `g` holds the
-// gradient w.r.t. the logits.
+// Sinkhorn backward by recompute with checkpoints.  The forward is
+// A_0 = softmax(m) + eps, B_t = colnorm(A_t), A_{t+1} = rownorm(B_t) and the
+// output is B_{steps-1}.  Only every K-th state is kept in `traj` (caller
+// scratch, sk_ckpt_count(N, iters) matrices of N*N floats, consecutive floats
+// `tstride` apart so a block can interleave threads): checkpoint 0 is A_0 and
+// checkpoint c >= 1 is B_{cK-1}.  The reverse sweep recomputes each segment of
+// K states into registers from its checkpoint with the same operations in the
+// same order, so every recomputed state equals the forward one bit for bit.
+// On entry `m` holds the logits and `g` the gradient w.r.t. the output; on
+// exit `g` holds the gradient w.r.t. the logits.
+template <int N>
+__host__ __device__ constexpr int sk_ckpt_every() { return N <= 4 ? 4 : 1; }
+
+__host__ __device__ inline int sk_ckpt_count(int n, int iters) {
+  const int steps = iters < 1 ? 1 : iters;
+  const int k = n <= 4 ? 4 : 1;
+  return (steps + k - 1) / k;
+}
+
 template <int N>
 __device__ void sinkhorn_bwd(const float (&m)[N * N], float (&g)[N * N], int iters, float eps,
                              float *traj, int tstride) {
+  constexpr int K = sk_ckpt_every<N>();
+  constexpr int NN = N * N;
   const int steps = iters < 1 ? 1 : iters;
-  float s0[N * N];
-MHC_UNROLL_N
-  for (int k = 0; k < N * N; ++k) s0[k] = m[k];
-  sk_softmax_rows<N>(s0);
-  float p[N * N];
-MHC_UNROLL_N
-  for (int k = 0; k < N * N; ++k) p[k] = s0[k] + eps;
-  // column-normalisation inputs (A_t) are stored; B_t = colnorm(A_t)
-MHC_UNROLL_N
-  for (int k = 0; k < N * N; ++k) traj[k * tstride] = p[k];
-  sk_col_norm<N>(p, eps);
-  for (int it = 1; it < steps; ++it) {
-    // A_it = rownorm(B_{it-1}) is stored; B_it = colnorm(A_it)
-    sk_row_norm<N>(p, eps);
-    float *slot = traj + (size_t)it * N * N * tstride;
-MHC_UNROLL_N
-    for (int k = 0; k < N * N; ++k) slot[k * tstride] = p[k];
-    sk_col_norm<N>(p, eps);
-  }
-  // reverse sweep
-  for (int it = steps - 1; it >= 1; --it) {
-    const float *slot = traj + (size_t)it * N * N * tstride;
-    float a[N * N];
-MHC_UNROLL_N
-    for (int k = 0; k < N * N; ++k) a[k] = slot[k * tstride];
-    sk_col_norm_bwd<N>(a, g, eps);  // through B_it = colnorm(A_it)
-    // recover B_{it-1}: it is the column-normalised A_{it-1}
-    const float *prev = traj + (size_t)(it - 1) * N * N * tstride;
-    float b[N * N];
-MHC_UNROLL_N
-    for (int k = 0; k < N * N; ++k) b[k] = prev[k * tstride];
-    sk_col_norm<N>(b, eps);
-    sk_row_norm_bwd<N>(b, g, eps);  // through A_it = rownorm(B_{it-1})
-  }
   {
-    float a[N * N];
+    float p[NN];
 MHC_UNROLL_N
-    for (int k = 0; k < N * N; ++k) a[k] = traj[k * tstride];
-    sk_col_norm_bwd<N>(a, g, eps);  // through B_0 = colnorm(A_0); dA_0 = dS_0
+    for (int k = 0; k < NN; ++k) p[k] = m[k];
+    sk_softmax_rows<N>(p);
+MHC_UNROLL_N
+    for (int k = 0; k < NN; ++k) {
+      p[k] += eps;  // A_0
+      traj[k * tstride] = p[k];
+    }
+    for (int it = 0; it + 1 < steps; ++it) {
+      sk_col_norm<N>(p, eps);  // B_it
+      if ((it + 1) % K == 0) {
+        float *slot = traj + (size_t)((it + 1) / K) * NN * tstride;
+MHC_UNROLL_N
+        for (int k = 0; k < NN; ++k) slot[k * tstride] = p[k];
+      }
+      sk_row_norm<N>(p, eps);  // A_{it+1}
+    }
   }
-  // softmax backward
+  // reverse sweep, one segment of K states at a time
+  for (int c = (steps + K - 1) / K - 1; c >= 0; --c) {
+    const int base = c * K;
+    const float *slot = traj + (size_t)c * NN * tstride;
+    float a[K][NN];  // A_base .. A_{base+K-1}
+MHC_UNROLL_N
+    for (int k = 0; k < NN; ++k) a[0][k] = slot[k * tstride];
+    if (c > 0) sk_row_norm<N>(a[0], eps);  // A_base = rownorm(B_{base-1})
+    // states past the last step are computed too (cheaper than a branch that
+    // keeps `a` out of registers) and never used
+#pragma unroll
+    for (int u = 1; u < K; ++u) {
+MHC_UNROLL_N
+      for (int k = 0; k < NN; ++k) a[u][k] = a[u - 1][k];
+      sk_col_norm<N>(a[u], eps);
+      sk_row_norm<N>(a[u], eps);
+    }
+#pragma unroll
+    for (int u = K - 1; u >= 1; --u) {
+      if (base + u < steps) {
+        sk_col_norm_bwd<N>(a[u], g, eps);  // through B_it = colnorm(A_it)
+        float b[NN];                       // B_{it-1} = colnorm(A_{it-1})
+MHC_UNROLL_N
+        for (int k = 0; k < NN; ++k) b[k] = a[u - 1][k];
+        sk_col_norm<N>(b, eps);
+        sk_row_norm_bwd<N>(b, g, eps);     // through A_it = rownorm(B_{it-1})
+      }
+    }
+    sk_col_norm_bwd<N>(a[0], g, eps);      // the segment's first state
+    if (c > 0) {
+      float b[NN];                         // B_{base-1}: the checkpoint itself
+MHC_UNROLL_N
+      for (int k = 0; k < NN; ++k) b[k] = slot[k * tstride];
+      sk_row_norm_bwd<N>(b, g, eps);
+    }
+  }
+  // softmax backward (dA_0 = dS_0)
+  float s0[NN];
+MHC_UNROLL_N
+  for (int k = 0; k < NN; ++k) s0[k] = m[k];
+  sk_softmax_rows<N>(s0);
 MHC_UNROLL_N
   for (int i = 0; i < N; ++i) {
     float dot = 0.f;

@@ -24,7 +24,7 @@ template <int N>
 __global__ void __launch_bounds__(128)
 sinkhorn_bwd_kernel(const void *__restrict__ M, int mdt, const void *__restrict__ dY, int gdt,
                     void *__restrict__ dM, int dmdt, int64_t batch, int iters, float eps, int TB) {
-  extern __shared__ float traj[];  // [steps][N*N][TB]
+  extern __shared__ float traj[];  // [checkpoints][N*N][TB]
   const int t = threadIdx.x;
   const int64_t b = (int64_t)blockIdx.x * TB + t;
   if (t >= TB || b >= batch) return;
@@ -40,8 +40,7 @@ MHC_UNROLL_N
 }
 
 size_t sinkhorn_bwd_smem_per_item(int n, int iters) {
-  const int steps = iters < 1 ? 1 : iters;
-  return (size_t)steps * n * n * 4;
+  return (size_t)sk_ckpt_count(n, iters) * n * n * 4;
 }
 
 cudaError_t launch_sinkhorn_fwd(int n, const void *M, int m_dtype, void *Y, int y_dtype,

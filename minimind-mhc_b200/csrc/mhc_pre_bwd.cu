@@ -5,7 +5,8 @@
 //     pass over x and dz, one warp per token with every load of a round in
 //     flight before the first FMA.
 //  K1 coef_bwd_kernel  : one thread per token runs the gate / Sinkhorn
-//     backward (the Sinkhorn trajectory is recomputed into shared memory) and
+//     backward (the Sinkhorn trajectory is recomputed, every 4th state kept in
+//     shared memory) and
 //     writes dm = dL/dmixes, the RMS-backward row coefficient and the
 //     aggregation weights.  Per-block sums of the alpha / bias gradients go to
 //     the workspace.  (Without K1a's dots it computes them itself, one warp per
@@ -39,8 +40,7 @@ PreBwdPlan plan_pre_bwd(int mode, int n, int64_t T, int C, int sk_iters, int sm_
   const int64_t nC = (int64_t)n * C;
   int tokens = 32;
   if (mode == FULL) {
-    const int steps = sk_iters < 1 ? 1 : sk_iters;
-    const size_t per = (size_t)steps * n * n * 4;
+    const size_t per = (size_t)sk_ckpt_count(n, sk_iters) * n * n * 4;
     const size_t budget = 96 * 1024;
     int t = (int)(budget / per);
     if (t < 1) t = (per <= 200 * 1024) ? 1 : 0;  // 0 => unsupported
@@ -159,7 +159,7 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
   float *par = smem;                     // [NPAR]
   float *dots = par + NPAR;              // [TB][N]
   float *pg = dots + TB * N;             // [TB][NG]
-  float *traj = pg + TB * NG;            // [steps][N*N][TB]
+  float *traj = pg + TB * NG;            // [checkpoints][N*N][TB]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tok0 = (int64_t)blockIdx.x * TB;
@@ -473,8 +473,8 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
         if (T > 0) {
           // K1
           const int TB = plan.k1_tokens;
-          const int steps = p.sk_iters < 1 ? 1 : p.sk_iters;
-          const size_t traj = (MODE == FULL && p.apply_sinkhorn) ? (size_t)steps * N * N * TB : 0;
+          const size_t traj =
+              (MODE == FULL && p.apply_sinkhorn) ? (size_t)sk_ckpt_count(N, p.sk_iters) * N * N * TB : 0;
           const size_t smem1 = ((size_t)(3 + 2 * N + N * N) + (size_t)TB * N + (size_t)TB * NG + traj) * 4;
           const bool vecok = C % VEC == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)dz & 15) == 0;
           // K1a: the dot products, a streaming pass with every SM busy

@@ -228,3 +228,24 @@ def test_cpu_tensors_are_rejected():
     mod = MHCConnection_Fused(4, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         mod(torch.randn(1, 4, 256), lambda z: z)
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+@pytest.mark.parametrize("iters", [1, 2, 3, 4, 5, 7, 10, 20, 21])
+def test_sinkhorn_backward_checkpoint_segments(n, iters):
+    """Sinkhorn-Knopp backward by recompute (states kept every 4th step for
+    n <= 4, then recomputed segment by segment) against fp64 autograd of the
+    oracle, at iteration counts that end on full and on partial segments."""
+    from model.mhc_fused import sinkhorn_normalize
+    gen = torch.Generator().manual_seed(n * 100 + iters)
+    m = torch.randn(257, n, n, generator=gen) * 0.7
+    dy = torch.randn(257, n, n, generator=gen)
+    md = m.to(DEV).requires_grad_(True)
+    y = sinkhorn_normalize(md, iters, 1e-6)
+    (dm,) = torch.autograd.grad(y, md, dy.to(DEV))
+    m64 = m.double().requires_grad_(True)
+    y64 = O.sinkhorn(m64, iters, 1e-6)
+    (dm64,) = torch.autograd.grad(y64, m64, dy.double())
+    assert (y.double().cpu() - y64).abs().max().item() < 2e-6
+    err = (dm.double().cpu() - dm64).abs().max().item()
+    assert err < 1e-5 + 1e-4 * dm64.abs().max().item(), err
