@@ -136,39 +136,51 @@ post_fwd_scalar_kernel(const void *__restrict__ x, int x_dt, const void *__restr
   }
 }
 
-// Backward, one warp per token.  Vector path (Tx / Tf packs).
+// Backward, one warp per token.  Vector path (Tx / Tf packs).  The token's
+// coefficients sit in a per-warp shared-memory slot (read by broadcast), which
+// leaves the registers to the accumulators and to one whole round of loads:
+// every lane issues its n dout vectors, n x vectors and its f vector before any
+// arithmetic.  At n = 4 that fits three 256-thread blocks per SM.
 template <int N, typename Tx, typename Tf, bool HAS_RES>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, N <= 4 ? 3 : 1)
 post_bwd_kernel(const Tx *__restrict__ dout, const Tx *__restrict__ x, const void *__restrict__ h_res,
                 int hr_dt, const void *__restrict__ h_post, int hp_dt, const Tf *__restrict__ f,
                 Tx *__restrict__ dx, void *__restrict__ dh_res, void *__restrict__ dh_post,
                 Tf *__restrict__ df, int64_t T, int C) {
   constexpr int VEC = 16 / sizeof(Tx);
+  constexpr int NR = HAS_RES ? N * N : 0;   // H_res entries
   constexpr int NH = HAS_RES ? N * N : 1;
+  constexpr int NCO = NR + N;                // H_res then H_post
+  __shared__ float cs_all[8][NCO];
   const int lane = threadIdx.x & 31;
+  float *cs = cs_all[threadIdx.x >> 5];
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t nC = (int64_t)N * C;
   const int vpt = C / VEC;
   for (int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < T;
        tok += nwarps) {
-    float H[NH], hp[N], aH[NH], ahp[N];
+    __syncwarp();  // the previous token's coefficient reads are done
+    for (int k = lane; k < NCO; k += 32)
+      cs[k] = k < NR ? load_dyn(h_res, hr_dt, tok * (N * N) + k) : load_dyn(h_post, hp_dt, tok * N + (k - NR));
+    __syncwarp();
+    const float *H = cs;
+    const float *hp = cs + NR;
+    float aH[NH], ahp[N];
     MHC_UNROLL_N
-    for (int k = 0; k < NH; ++k) {
-      H[k] = HAS_RES ? load_dyn(h_res, hr_dt, tok * (N * N) + k) : 0.f;
-      aH[k] = 0.f;
-    }
+    for (int k = 0; k < NH; ++k) aH[k] = 0.f;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      hp[i] = load_dyn(h_post, hp_dt, tok * N + i);
-      ahp[i] = 0.f;
-    }
+    for (int i = 0; i < N; ++i) ahp[i] = 0.f;
     const Tx *gr = dout + tok * nC;
     const Tx *xr = x + tok * nC;
     for (int v = lane; v < vpt; v += 32) {
       const int64_t off = (int64_t)v * VEC;
-      Pack<Tx> pg[N];
+      Pack<Tx> pg[N], px[HAS_RES ? N : 1];
 #pragma unroll
       for (int i = 0; i < N; ++i) pg[i].raw = ldg_stream(gr + (int64_t)i * C + off);
+      if constexpr (HAS_RES) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) px[j].raw = ldg_stream(xr + (int64_t)j * C + off);
+      }
       float fv[VEC];
       load_vec_stream<Tf, VEC>(f + tok * C + off, fv);
 #pragma unroll
@@ -190,12 +202,10 @@ post_bwd_kernel(const Tx *__restrict__ dout, const Tx *__restrict__ x, const voi
         // dH_res[i][j] += <g_i, x_j>;  dx_j = sum_i H[i][j] g_i
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          Pack<Tx> px;
-          px.raw = ldg_stream(xr + (int64_t)j * C + off);
 #pragma unroll
           for (int i = 0; i < N; ++i)
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) aH[i * N + j] = fmaf(pg[i].get(e), px.get(e), aH[i * N + j]);
+            for (int e = 0; e < VEC; ++e) aH[i * N + j] = fmaf(pg[i].get(e), px[j].get(e), aH[i * N + j]);
           if (dx) {
             Pack<Tx> o;
 #pragma unroll
@@ -377,7 +387,7 @@ cudaError_t launch_post_bwd(int n, int x_dtype, const void *dout, const void *x,
   const int xvec = x_dtype == MHC_F32 ? 4 : 8;
   const bool vecok = is_vec_pair(x_dtype, f_dtype) && C % xvec == 0 && a16(x) && a16(dout) &&
                      a16(f) && a16(dx) && a16(df);
-  const unsigned grid = grid_for(T * 32, 256, sms, 8);
+  const unsigned grid = grid_for(T * 32, 256, sms, 6);
   return with_n(n, [&](auto nn) {
     constexpr int N = decltype(nn)::value;
     auto go = [&](auto kern, auto... args) {
