@@ -66,7 +66,7 @@ struct BCfg {
 };
 
 // barrier slots
-constexpr int B_XF = 0, B_XE = XS, B_SR = 2 * XS, B_PF = 3 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
+constexpr int B_XF = 0, B_XE = XS, B_PF = 2 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
               B_DRAIN = B_DE + 2, NBARS = B_DRAIN + 1;
 
 // A of the dx product: 8-row groups are padded by one 16-byte granule so the
@@ -128,7 +128,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 template <int N, int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap amap,
-                  const __grid_constant__ CUtensorMap dmap, BArgs a) {
+                  BArgs a) {
   using Cf = BCfg<N, MODE>;
   constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2;
   extern __shared__ uint8_t smem_raw[];
@@ -156,8 +156,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     *abort_flag = 0;
     for (int i = 0; i < XS; ++i) {
       mbar_init(BAR(B_XF + i), 1);
-      mbar_init(BAR(B_XE + i), 2);         // MMA commit + the dx store has read the stage
-      mbar_init(BAR(B_SR + i), NEPI);      // every epilogue warp wrote its dx part into the stage
+      mbar_init(BAR(B_XE + i), 1 + NEPI);  // MMA commit + every epilogue warp (x read, dx written back)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(B_PF + b), NPREP);
@@ -393,28 +392,30 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         }
       }
       tc_fence_before();
-      fence_proxy_async_smem();  // dx written through the generic proxy, read by the TMA store
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(BAR(B_DE + b));
-        mbar_arrive(BAR(B_SR + s));
-      }
-      // one thread stores the tile's dx with two TMA boxes (rows past T are
-      // clipped by the tensor map), then frees the stage once they are read
-      if (warp == W_EPI) {
-        int good = 1;
-        if (lane == 0) {
-          good = wait_parity<false>(BAR(B_SR + s), (uint32_t)(lt / XS) & 1u, abort_flag) ? 1 : 0;
-          if (good) {
-            const int t0 = (int)((tile_beg + lt) * TM);
-            tma_store_2d(&dmap, base_u32 + L.xs + s * XSTAGE + 2 * CHUNK, col0, t0);
-            tma_store_2d(&dmap, base_u32 + L.xs + s * XSTAGE + 3 * CHUNK, col0 + 64, t0);
-            bulk_commit();
-            bulk_wait_read0();
-            mbar_arrive(BAR(B_XE + s));
-          }
+      __syncwarp();  // the warp's 32 x 64 dx block is complete in shared memory
+      if (lane == 0) mbar_arrive(BAR(B_DE + b));
+      // coalesced write-back of the warp's own block: an instruction stores
+      // 4 whole 128-byte row segments (lane -> row k*4 + lane/8, granule lane%8)
+      {
+        const int gq = lane & 7;
+        const uint8_t *blk = base + L.xs + s * XSTAGE + (2 + half) * CHUNK;
+        __nv_bfloat16 *dxb = a.dx + col0 + half * 64 + gq * 8;
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = quad * 32 + k * 4 + (lane >> 3);
+          v[k] = *reinterpret_cast<const uint4 *>(blk + r * 128 + ((gq ^ (r & 7)) << 4));
         }
-        if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = quad * 32 + k * 4 + (lane >> 3);
+          const int64_t tk = (tile_beg + lt) * TM + r;
+          if (tk < tok_end) __stcs(reinterpret_cast<uint4 *>(dxb + tk * a.nC), v[k]);
+        }
+        // the loads above have returned (the stores consumed them): only now
+        // may the producer refill the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(B_XE + s));
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
@@ -423,7 +424,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       wgt = wgt_n;
     }
     if (!ok) record_error(ERR_EPI, abort_flag);
-    if (warp == W_EPI && lane == 0) bulk_wait0();  // every dx store has completed
     // dphi partial of this CTA: D2 lanes are its columns
     if (half == 0) {
       const bool drained = WAIT_WARP(BAR(B_DRAIN), 0u);
@@ -494,14 +494,14 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   // x and dx_add as (T rows) x (nC columns): 128-row x 64-column boxes, 128-byte swizzle
-  CUtensorMap tmap, amap, dmap;
+  CUtensorMap tmap, amap;
   const cuuint64_t dims[2] = {(cuuint64_t)a.nC, (cuuint64_t)a.T};
   const cuuint64_t strides[1] = {(cuuint64_t)a.nC * 2};
   const cuuint32_t box[2] = {64, (cuuint32_t)TM};
   const cuuint32_t estr[2] = {1, 1};
-  const void *srcs[3] = {x, a.dx_add ? (const void *)a.dx_add : x, a.dx};
-  CUtensorMap *maps[3] = {&tmap, &amap, &dmap};
-  for (int m = 0; m < 3; ++m)
+  const void *srcs[2] = {x, a.dx_add ? (const void *)a.dx_add : x};
+  CUtensorMap *maps[2] = {&tmap, &amap};
+  for (int m = 0; m < 2; ++m)
     if (enc(maps[m], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(srcs[m]), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -518,7 +518,7 @@ static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t str
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   (void)sms;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, amap, dmap, a);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, amap, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
