@@ -65,6 +65,23 @@ struct BCfg {
   static constexpr int NB2 = ((2 * FD + 15) / 16) * 16;  // dphi product N
 };
 
+// Per-tile timeline instrumentation (global timer, block 0), compiled in only
+// with -DMHC_TCB_TRACE; events are indexed [local tile][event].
+#ifdef MHC_TCB_TRACE
+__device__ long long g_tcb_trace[64][16];
+__device__ unsigned long long g_tcb_t0 = ~0ull;
+__device__ __forceinline__ unsigned long long tcb_gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TCB_TRACE(lt_, ev) do { if (blockIdx.x == 0 && (lt_) < 64) g_tcb_trace[lt_][ev] = (long long)tcb_gtimer(); } while (0)
+#else
+#define TCB_TRACE(lt_, ev) do { } while (0)
+#endif
+enum TcbEv { E_P_ISSUE, E_M_PF, E_M_XF, E_M_GO, E_PREP_DONE, E_EPI_GO, E_EPI_END, E_EPI_MID, E_EPI_LAST };
+constexpr int TCB_NEV = 16;
+
 // barrier slots
 constexpr int B_XF = 0, B_XE = XS, B_PF = 2 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
               B_DRAIN = B_DE + 2, NBARS = B_DRAIN + 1;
@@ -190,6 +207,9 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
   }
   fence_proxy_async_smem();
   __syncthreads();
+#ifdef MHC_TCB_TRACE
+  if (threadIdx.x == 0) atomicMin(&g_tcb_t0, tcb_gtimer());
+#endif
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
 
   if (warp == W_PROD) {
@@ -199,6 +219,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       for (; lt < ntile && ok; ++lt) {
         const int s = lt % XS;
         if (!wait_parity<false>(BAR(B_XE + s), ((uint32_t)(lt / XS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+        TCB_TRACE(lt, E_P_ISSUE);
         mbar_arrive_expect_tx(BAR(B_XF + s), a.dx_add ? XSTAGE : 2 * CHUNK);
         const int t0 = (int)((tile_beg + lt) * TM);
         tma_load_2d(base_u32 + L.xs + s * XSTAGE, &tmap, col0, t0, BAR(B_XF + s));
@@ -223,8 +244,11 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         const int b = lt & 1, s = lt % XS;
         const uint32_t bph = (uint32_t)(lt >> 1) & 1u;
         if (!wait_parity<false>(BAR(B_PF + b), bph, abort_flag)) { ok = false; break; }
+        TCB_TRACE(lt, E_M_PF);
         if (!wait_parity<false>(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u, abort_flag)) { ok = false; break; }
+        TCB_TRACE(lt, E_M_XF);
         if (!wait_parity<false>(BAR(B_DE + b), bph ^ 1u, abort_flag)) { ok = false; break; }
+        TCB_TRACE(lt, E_M_GO);
         tc_fence_after();
         // dx product into D1[b]
         const uint32_t a1 = base_u32 + L.a1 + (uint32_t)b * (TM / 8) * a1_sbo(K1);
@@ -319,6 +343,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       fence_proxy_async_smem();  // generic writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(B_PF + b));
+      if (warp == W_PREP && lane == 0) TCB_TRACE(lt, E_PREP_DONE);
     }
     if (!ok) record_error(ERR_PREP, abort_flag);
   } else {
@@ -353,6 +378,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       load_next(lt + 1, dzn, inv_n, rowb_n, wgt_n);
       if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt >> 1) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
+      if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_GO);
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
       uint8_t *arow = base + L.xs + s * XSTAGE + (2 + half) * CHUNK + row * 128;  // dx_add tile; dx goes back here
@@ -391,6 +417,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
           }
         }
       }
+      if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_MID);
       tc_fence_before();
       __syncwarp();  // the warp's 32 x 64 dx block is complete in shared memory
       if (lane == 0) mbar_arrive(BAR(B_DE + b));
@@ -416,6 +443,8 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         // may the producer refill the stage
         __syncwarp();
         if (lane == 0) mbar_arrive(BAR(B_XE + s));
+        if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_END);
+        if (lane == 0) TCB_TRACE(lt, 8 + e);
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
