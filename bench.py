@@ -448,12 +448,238 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Model-level workloads
+# ---------------------------------------------------------------------------
+
+def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=4, inter=2048, vocab=6400,
+                   experts=8, topk=2, theta=1e6, eps=1e-6, iters=20):
+    """A MiniMind-3-style decoder written for this benchmark (random init
+    N(0, 0.02)): embedding -> RMSNorm -> StreamExpand, then per layer an
+    attention and an MLP (or top-2 MoE) sublayer, each wrapped in this build's
+    MHCConnection_Fused with a pre-norm closure (the call-site structure of
+    model_minimind.py:315-340), then MHCHead -> RMSNorm -> tied LM head.
+    Attention: GQA with q/k RMSNorm and RoPE, torch SDPA (causal)."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    from model.mhc_common import MHCHead, StreamExpand
+    from model.mhc_fused import MHCConnection_Fused
+
+    hd = hidden // heads
+
+    class Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q = nn.Linear(hidden, heads * hd, bias=False)
+            self.k = nn.Linear(hidden, kv_heads * hd, bias=False)
+            self.v = nn.Linear(hidden, kv_heads * hd, bias=False)
+            self.o = nn.Linear(heads * hd, hidden, bias=False)
+            self.qn = nn.RMSNorm(hd, eps=eps)
+            self.kn = nn.RMSNorm(hd, eps=eps)
+
+        def forward(self, x, cos, sin):
+            b, l, _ = x.shape
+            q = self.qn(self.q(x).view(b, l, heads, hd))
+            k = self.kn(self.k(x).view(b, l, kv_heads, hd))
+            v = self.v(x).view(b, l, kv_heads, hd)
+
+            def rope(t):
+                h = t.shape[-1] // 2
+                rot = torch.cat((-t[..., h:], t[..., :h]), dim=-1)
+                return (t * cos + rot * sin).to(t.dtype)
+
+            q, k = rope(q), rope(k)
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               is_causal=True, enable_gqa=True)
+            return self.o(o.transpose(1, 2).reshape(b, l, heads * hd))
+
+    class SwiGLU(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.g = nn.Linear(hidden, inter, bias=False)
+            self.u = nn.Linear(hidden, inter, bias=False)
+            self.d = nn.Linear(inter, hidden, bias=False)
+
+        def forward(self, x):
+            return self.d(F.silu(self.g(x)) * self.u(x))
+
+    class MoE(nn.Module):
+        """Softmax router, top-k experts, weights renormalised over the k."""
+        def __init__(self):
+            super().__init__()
+            self.router = nn.Linear(hidden, experts, bias=False)
+            self.experts = nn.ModuleList([SwiGLU() for _ in range(experts)])
+
+        def forward(self, x):
+            shape = x.shape
+            xf = x.reshape(-1, hidden)
+            w, idx = torch.softmax(self.router(xf).float(), dim=-1).topk(topk, dim=-1)
+            w = w / (w.sum(dim=-1, keepdim=True) + 1e-20)
+            flat = idx.flatten()
+            order = flat.argsort()
+            tok = order // topk
+            counts = torch.bincount(flat, minlength=experts).tolist()
+            xs = xf.index_select(0, tok)
+            # each expert's rows are zero-padded to a multiple of 256, so the
+            # GEMM shapes come from a small set (new shapes every step would
+            # send the GEMM library back to its host-side selection each time)
+            outs = []
+            for e, c in zip(self.experts, xs.split(counts)):
+                if c.shape[0] == 0:
+                    continue
+                pad = (-c.shape[0]) % 256
+                outs.append(e(F.pad(c, (0, 0, 0, pad)))[:c.shape[0]] if pad else e(c))
+            ys = torch.cat(outs) if outs else xs[:0]
+            ys = ys * w.flatten()[order].unsqueeze(1).to(ys.dtype)
+            return torch.zeros_like(xf).index_add_(0, tok, ys).view(shape)
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.attn, self.mlp = Attn(), (MoE() if moe else SwiGLU())
+            self.n1, self.n2 = nn.RMSNorm(hidden, eps=eps), nn.RMSNorm(hidden, eps=eps)
+            self.attn_mhc = MHCConnection_Fused(n, hidden, eps=eps, sinkhorn_iters=iters)
+            self.mlp_mhc = MHCConnection_Fused(n, hidden, eps=eps, sinkhorn_iters=iters)
+
+        def forward(self, h, cos, sin):
+            h = self.attn_mhc(h, lambda z: self.attn(self.n1(z), cos, sin))
+            return self.mlp_mhc(h, lambda z: self.mlp(self.n2(z)))
+
+    class Decoder(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.emb = nn.Embedding(vocab, hidden)
+            self.entry = nn.Sequential(nn.RMSNorm(hidden, eps=eps), StreamExpand(n, hidden))
+            self.blocks = nn.ModuleList([Block() for _ in range(layers)])
+            self.exit = nn.Sequential(MHCHead(n, hidden, eps=eps), nn.RMSNorm(hidden, eps=eps))
+            self.head = nn.Linear(hidden, vocab, bias=False)
+            self.head.weight = self.emb.weight
+
+        def forward(self, ids):
+            l = ids.shape[1]
+            pos = torch.arange(l, device=ids.device, dtype=torch.float32)
+            inv = 1.0 / (theta ** (torch.arange(0, hd, 2, device=ids.device, dtype=torch.float32) / hd))
+            ang = torch.outer(pos, inv)
+            cos = torch.cat([ang.cos(), ang.cos()], dim=-1)[None, :, None, :]
+            sin = torch.cat([ang.sin(), ang.sin()], dim=-1)[None, :, None, :]
+            h = self.entry(self.emb(ids))
+            for blk in self.blocks:
+                h = blk(h, cos, sin)
+            return self.head(self.exit(h))
+
+    m = Decoder()
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if p.dim() >= 2 and "mhc" not in name and "exit.0" not in name:
+                p.normal_(0.0, 0.02)
+    m = m.to(dev, torch.bfloat16)
+    # mHC parameters and their gradients stay fp32 (fp32 coefficient math)
+    for mod in m.modules():
+        if isinstance(mod, (MHCConnection_Fused, MHCHead)):
+            mod.float()
+    return m
+
+
+def run_model(args, rank, world, local_rank):
+    """configs[3] (--workload c4): forward of the 8-layer decoder, 32 x 2048
+    tokens per GPU.  configs[4] (--workload c5): training step (forward,
+    backward, one NCCL all-reduce of all gradients in a flat bucket, AdamW) of
+    the MoE variant, 8 x 2048 tokens per GPU (global 64 x 2048 at 8 GPUs).
+    Weak scaling; token ids uniform over the vocabulary; CUDA-event timing,
+    max over ranks."""
+    import torch.nn.functional as F
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    train = args.workload == "c5"
+    torch.manual_seed(1234 + rank)
+    model = _build_decoder(moe=train, dev=dev)
+    batch = 8 if train else 32
+    seq = 2048
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    ids = torch.randint(0, 6400, (batch, seq), device=dev, generator=gen)
+    labels = torch.randint(0, 6400, (batch, seq), device=dev, generator=gen)
+    params = [p for p in model.parameters()]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True) if train else None
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def step():
+        if not train:
+            with torch.no_grad():
+                model(ids)
+            return
+        logits = model(ids)
+        loss = F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), labels.view(-1))
+        loss.backward()
+        if world > 1:
+            # one flat bucket per dtype: the mHC (fp32) and the rest (bf16)
+            for dt in (torch.float32, torch.bfloat16):
+                gs = [p.grad for p in params if p.grad is not None and p.grad.dtype == dt]
+                if not gs:
+                    continue
+                flat = torch.cat([g.reshape(-1) for g in gs])
+                dist.all_reduce(flat)
+                flat.div_(world)
+                off = 0
+                for g in gs:
+                    g.copy_(flat[off:off + g.numel()].view_as(g))
+                    off += g.numel()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(dev)
+    sampler.start()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    if rank != 0:
+        return
+    tokens = batch * seq
+    value = world * tokens * args.steps / (ms / 1e3)
+    line = {
+        "metric": "model training tokens/s" if train else "model forward tokens/s", "value": value,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (token ids uniform over the vocabulary, random-init weights)",
+        "config": {
+            "workload": ("config5: MiniMind MoE (8 experts, top-2) + mHC training step (fwd + bwd + grad "
+                         "all-reduce + AdamW)" if train else
+                         "config4: dense MiniMind-3-style decoder + mHC forward"),
+            "model": "hidden 768, 8 layers, 8 q / 4 kv heads, RoPE 1e6, SwiGLU 2048, vocab 6400, n=4, "
+                     "20 Sinkhorn iterations",
+            "global_batch": world * batch, "seq_len": seq, "parallelism": f"dp{world}",
+        },
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["layer", "c4", "c5"], default="layer",
+                    help="layer: configs[1] mHC layer (the headline); c4 / c5: model-level configs[3] / [4]")
     ap.add_argument("--variant", choices=["full", "nohres"], default="full")
     ap.add_argument("--C", type=int, default=0, help="stream width for --variant nohres (768 or 1024)")
     ap.add_argument("--tokens", type=int, default=16 * 2048)
@@ -482,7 +708,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "layer":
+            run_ours(args, rank, world, local_rank)
+        else:
+            run_model(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
