@@ -521,14 +521,14 @@ def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=
             tok = order // topk
             counts = torch.bincount(flat, minlength=experts).tolist()
             xs = xf.index_select(0, tok)
-            # each expert's rows are zero-padded to a multiple of 256, so the
+            # each expert's rows are zero-padded to a multiple of 1024, so the
             # GEMM shapes come from a small set (new shapes every step would
             # send the GEMM library back to its host-side selection each time)
             outs = []
             for e, c in zip(self.experts, xs.split(counts)):
                 if c.shape[0] == 0:
                     continue
-                pad = (-c.shape[0]) % 256
+                pad = (-c.shape[0]) % 1024
                 outs.append(e(F.pad(c, (0, 0, 0, pad)))[:c.shape[0]] if pad else e(c))
             ys = torch.cat(outs) if outs else xs[:0]
             ys = ys * w.flatten()[order].unsqueeze(1).to(ys.dtype)
