@@ -21,10 +21,13 @@
 //     from the TMA-staged x tile as an MN-major operand (the tile's 128-byte
 //     rows are tokens, i.e. K), B = [inv*dm hi ; lo] with tokens along K.
 //
-// Warp roles: 0 TMA producer of the x and dx_add tiles (2 stages), 1 MMA
-// issuer, 2-9 the dx epilogue (thread = token row = TMEM lane, two warps per
-// lane quadrant, 64 columns each; dz is loaded one tile ahead), 10-13 prep
-// warps (thread = token row).  All hand-offs are
+// Warp roles: 0 TMA producer of the x tiles (3 stages), 1 MMA issuer, 2 TMA
+// producer of the dx_add tiles (2 buffers, which then receive dx), 3-10 the dx
+// epilogue (thread = token row = TMEM lane, two warps per lane quadrant, 64
+// columns each; dz and the per-token scalars are loaded one tile ahead; an x
+// stage is released after the arithmetic, a dx buffer after its coalesced
+// write-back), 11-14 prep warps (thread = token row; their operand buffers are
+// single or double, whichever fits).  All hand-offs are
 // mbarriers; every wait is bounded and a timeout sets the device error word.
 // The per-CTA dphi partials go to workspace and are summed in a fixed order
 // by the reduction kernel, so the result is deterministic.
@@ -48,27 +51,46 @@ using namespace sm100;
 
 constexpr int TM = 128;                 // tokens per tile
 constexpr int KCOL = 128;               // columns of n*C per CTA
-constexpr int XS = 2;                   // tile stages (x and dx_add)
+constexpr int XS = 3;                   // x tile stages
+constexpr int AS = 2;                   // dx_add / dx tile buffers
 constexpr int NEPI = 8, NPREP = 4;
-constexpr int W_PROD = 0, W_MMA = 1, W_EPI = 2, W_PREP = W_EPI + NEPI;
+constexpr int W_PROD = 0, W_MMA = 1, W_APROD = 2, W_EPI = 3, W_PREP = W_EPI + NEPI;
 constexpr int NWARPS = W_PREP + NPREP, NTHREADS = NWARPS * 32;
 constexpr int CHUNK = TM * 128;         // 128 rows x 64 bf16 columns (128-byte swizzle)
-constexpr int XSTAGE = 4 * CHUNK;       // x then dx_add, the CTA's 128 columns of one tile each
-constexpr int TMEM_COLS = 512;          // D1 x 2 at columns 0 / 128, D2 at 256
+constexpr int XSTAGE = 2 * CHUNK;       // the CTA's 128 columns of one tile (x, or dx_add then dx)
+constexpr int DB = 2;                   // dx accumulators in TMEM (one tile each; 3 measured no faster)
+constexpr int D2COL = DB * 128;         // the dphi accumulator follows them
+constexpr int TMEM_COLS = 512;          // D1 x DB at columns 0, 128, ..., then D2 (N <= 128)
 
 enum ErrCode { ERR_PROD = 11, ERR_MMA = 12, ERR_EPI = 13, ERR_PREP = 14 };
+
+// A of the dx product: 8-row groups are padded by one 16-byte granule so the
+// prep threads' row writes do not collide on shared-memory banks
+__host__ __device__ constexpr uint32_t a1_sbo(int K1) { return (uint32_t)(K1 / 8) * 128u + 16u; }
+
+constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block on sm_100
+
+__host__ __device__ constexpr uint32_t blayout_bytes(int K1, int NB2, int PB) {
+  return (uint32_t)(XS + AS) * XSTAGE + (uint32_t)KCOL * K1 * 2 + (uint32_t)PB * (TM / 8) * a1_sbo(K1) +
+         (uint32_t)PB * NB2 * TM * 2 + 512u;
+}
 
 template <int N, int MODE>
 struct BCfg {
   static constexpr int FD = Dims<N, MODE>::FD;
   static constexpr int K1 = ((3 * FD + 15) / 16) * 16;   // dx product K
   static constexpr int NB2 = ((2 * FD + 15) / 16) * 16;  // dphi product N
+  // prep operand buffers: two when they fit beside the x / dx rings, else one
+  static constexpr int PB = blayout_bytes(K1, NB2, 2) + 1024 <= SMEM_LIMIT ? 2 : 1;
+  static_assert(NB2 <= TMEM_COLS - D2COL, "dphi accumulator must fit after the dx accumulators");
 };
 
 // Per-tile timeline instrumentation (global timer, block 0), compiled in only
 // with -DMHC_TCB_TRACE; events are indexed [local tile][event].
 #ifdef MHC_TCB_TRACE
 __device__ long long g_tcb_trace[64][16];
+__device__ long long g_tcb_trace2[64][8];
+__device__ long long g_tcb_trace3[64][8];
 __device__ unsigned long long g_tcb_t0 = ~0ull;
 __device__ __forceinline__ unsigned long long tcb_gtimer() {
   unsigned long long t;
@@ -80,27 +102,23 @@ __device__ __forceinline__ unsigned long long tcb_gtimer() {
 #define TCB_TRACE(lt_, ev) do { } while (0)
 #endif
 enum TcbEv { E_P_ISSUE, E_M_PF, E_M_XF, E_M_GO, E_PREP_DONE, E_EPI_GO, E_EPI_END, E_EPI_MID, E_EPI_LAST };
-constexpr int TCB_NEV = 16;
 
 // barrier slots
-constexpr int B_XF = 0, B_XE = XS, B_PF = 2 * XS, B_PE = B_PF + 2, B_DF = B_PE + 2, B_DE = B_DF + 2,
-              B_DRAIN = B_DE + 2, NBARS = B_DRAIN + 1;
-
-// A of the dx product: 8-row groups are padded by one 16-byte granule so the
-// prep threads' row writes do not collide on shared-memory banks
-__host__ __device__ constexpr uint32_t a1_sbo(int K1) { return (uint32_t)(K1 / 8) * 128u + 16u; }
+constexpr int B_XF = 0, B_XE = XS, B_AF = 2 * XS, B_AE = B_AF + AS, B_PF = B_AE + AS, B_PE = B_PF + 2,
+              B_DF = B_PE + 2, B_DE = B_DF + DB, B_DRAIN = B_DE + DB, NBARS = B_DRAIN + 1;
 
 struct BLayout {
-  uint32_t xs, b1, a1, b2, bar, tmem, abort, total;
+  uint32_t xs, as, b1, a1, b2, bar, tmem, abort, total;
 };
 
-__host__ __device__ inline BLayout make_blayout(int K1, int NB2) {
+__host__ __device__ inline BLayout make_blayout(int K1, int NB2, int PB) {
   BLayout L;
   uint32_t o = 0;
   L.xs = o;    o += XS * XSTAGE;
+  L.as = o;    o += AS * XSTAGE;
   L.b1 = o;    o += (uint32_t)KCOL * K1 * 2;
-  L.a1 = o;    o += 2u * (TM / 8) * a1_sbo(K1);
-  L.b2 = o;    o += 2u * NB2 * TM * 2;
+  L.a1 = o;    o += (uint32_t)PB * (TM / 8) * a1_sbo(K1);
+  L.b2 = o;    o += (uint32_t)PB * NB2 * TM * 2;
   L.bar = o;   o += NBARS * 8;
   L.tmem = o;  o += 4;
   L.abort = o; o += 4;
@@ -147,12 +165,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap amap,
                   BArgs a) {
   using Cf = BCfg<N, MODE>;
-  constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2;
+  constexpr int FD = Cf::FD, K1 = Cf::K1, NB2 = Cf::NB2, PB = Cf::PB;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t *base = smem_raw + (base_u32 - raw_u32);
-  const BLayout L = make_blayout(K1, NB2);
+  const BLayout L = make_blayout(K1, NB2, PB);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(base + L.abort);
   const uint32_t bar0 = base_u32 + L.bar;
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
@@ -173,11 +191,17 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     *abort_flag = 0;
     for (int i = 0; i < XS; ++i) {
       mbar_init(BAR(B_XF + i), 1);
-      mbar_init(BAR(B_XE + i), 1 + NEPI);  // MMA commit + every epilogue warp (x read, dx written back)
+      mbar_init(BAR(B_XE + i), 1 + NEPI);  // MMA commit + every epilogue warp has read the x tile
+    }
+    for (int i = 0; i < AS; ++i) {
+      mbar_init(BAR(B_AF + i), 1);
+      mbar_init(BAR(B_AE + i), NEPI);      // every epilogue warp has written its dx block back
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(B_PF + b), NPREP);
       mbar_init(BAR(B_PE + b), 1);
+    }
+    for (int b = 0; b < DB; ++b) {
       mbar_init(BAR(B_DF + b), 1);
       mbar_init(BAR(B_DE + b), NEPI);
     }
@@ -212,26 +236,34 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
 #endif
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
 
-  if (warp == W_PROD) {
+  if (warp == W_PROD || warp == W_APROD) {
+    // x tiles (warp W_PROD) and dx_add tiles (warp W_APROD) stream through
+    // rings of their own depth, one issuing thread each
     if (lane == 0) {
+      const bool is_x = warp == W_PROD;
+      const int NS = is_x ? XS : AS;
+      const int bf = is_x ? B_XF : B_AF, be = is_x ? B_XE : B_AE;
+      const uint32_t ring = base_u32 + (is_x ? L.xs : L.as);
+      const CUtensorMap *map = is_x ? &tmap : &amap;
+      const bool load = is_x || a.dx_add != nullptr;
       bool ok = true;
       int lt = 0;
       for (; lt < ntile && ok; ++lt) {
-        const int s = lt % XS;
-        if (!wait_parity<false>(BAR(B_XE + s), ((uint32_t)(lt / XS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-        TCB_TRACE(lt, E_P_ISSUE);
-        mbar_arrive_expect_tx(BAR(B_XF + s), a.dx_add ? XSTAGE : 2 * CHUNK);
-        const int t0 = (int)((tile_beg + lt) * TM);
-        tma_load_2d(base_u32 + L.xs + s * XSTAGE, &tmap, col0, t0, BAR(B_XF + s));
-        tma_load_2d(base_u32 + L.xs + s * XSTAGE + CHUNK, &tmap, col0 + 64, t0, BAR(B_XF + s));
-        if (a.dx_add) {
-          tma_load_2d(base_u32 + L.xs + s * XSTAGE + 2 * CHUNK, &amap, col0, t0, BAR(B_XF + s));
-          tma_load_2d(base_u32 + L.xs + s * XSTAGE + 3 * CHUNK, &amap, col0 + 64, t0, BAR(B_XF + s));
+        const int s = lt % NS;
+        if (!wait_parity<false>(BAR(be + s), ((uint32_t)(lt / NS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+        if (is_x) TCB_TRACE(lt, E_P_ISSUE);
+        if (!load) {
+          mbar_arrive(BAR(bf + s));  // no dx_add: the buffer only receives dx
+          continue;
         }
+        mbar_arrive_expect_tx(BAR(bf + s), XSTAGE);
+        const int t0 = (int)((tile_beg + lt) * TM);
+        tma_load_2d(ring + s * XSTAGE, map, col0, t0, BAR(bf + s));
+        tma_load_2d(ring + s * XSTAGE + CHUNK, map, col0 + 64, t0, BAR(bf + s));
       }
       if (!ok) record_error(ERR_PROD, abort_flag);
-      const int l0 = lt > XS ? lt - XS : 0;
-      for (int p = l0; p < lt; ++p) wait_parity<false>(BAR(B_XF + p % XS), (uint32_t)(p / XS) & 1u, nullptr);
+      const int l0 = lt > NS ? lt - NS : 0;
+      for (int p = l0; p < lt; ++p) wait_parity<false>(BAR(bf + p % NS), (uint32_t)(p / NS) & 1u, nullptr);
     }
     __syncwarp();
   } else if (warp == W_MMA) {
@@ -241,9 +273,9 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       const uint32_t sbo1 = (uint32_t)(K1 / 8) * 128u;
       bool ok = true;
       for (int lt = 0; lt < ntile && ok; ++lt) {
-        const int b = lt & 1, s = lt % XS;
-        const uint32_t bph = (uint32_t)(lt >> 1) & 1u;
-        if (!wait_parity<false>(BAR(B_PF + b), bph, abort_flag)) { ok = false; break; }
+        const int b = lt % DB, s = lt % XS, pb = lt % PB;
+        const uint32_t bph = (uint32_t)(lt / DB) & 1u;
+        if (!wait_parity<false>(BAR(B_PF + pb), (uint32_t)(lt / PB) & 1u, abort_flag)) { ok = false; break; }
         TCB_TRACE(lt, E_M_PF);
         if (!wait_parity<false>(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u, abort_flag)) { ok = false; break; }
         TCB_TRACE(lt, E_M_XF);
@@ -251,7 +283,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         TCB_TRACE(lt, E_M_GO);
         tc_fence_after();
         // dx product into D1[b]
-        const uint32_t a1 = base_u32 + L.a1 + (uint32_t)b * (TM / 8) * a1_sbo(K1);
+        const uint32_t a1 = base_u32 + L.a1 + (uint32_t)pb * (TM / 8) * a1_sbo(K1);
         const uint32_t b1 = base_u32 + L.b1;
 #pragma unroll
         for (int ks = 0; ks < K1 / 16; ++ks)
@@ -261,13 +293,13 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         // two 64-column chunks 16 KB apart), B = inv*dm (MN-major, 8-feature
         // blocks TM*16 bytes apart), tokens along K for both
         const uint32_t xa = base_u32 + L.xs + s * XSTAGE;
-        const uint32_t b2 = base_u32 + L.b2 + (uint32_t)b * NB2 * TM * 2;
+        const uint32_t b2 = base_u32 + L.b2 + (uint32_t)pb * NB2 * TM * 2;
 #pragma unroll
         for (int ks = 0; ks < TM / 16; ++ks)
-          umma_bf16(tmem_base + 256u, umma_desc(xa + ks * 2048, CHUNK, 1024, 2),
+          umma_bf16(tmem_base + (uint32_t)D2COL, umma_desc(xa + ks * 2048, CHUNK, 1024, 2),
                     umma_desc(b2 + ks * 256, 128, TM * 16, 0), idesc2, (lt | ks) != 0 ? 1u : 0u);
         umma_commit(BAR(B_DF + b));
-        umma_commit(BAR(B_PE + b));
+        umma_commit(BAR(B_PE + pb));
         umma_commit(BAR(B_XE + s));
       }
       if (!ok) record_error(ERR_MMA, abort_flag);
@@ -279,8 +311,8 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     const int row = tid - W_PREP * 32;
     bool ok = true;
     for (int lt = 0; lt < ntile && ok; ++lt) {
-      const int b = lt & 1;
-      if (!WAIT_WARP(BAR(B_PE + b), ((uint32_t)(lt >> 1) & 1u) ^ 1u)) { ok = false; break; }
+      const int b = lt % PB;
+      if (!WAIT_WARP(BAR(B_PE + b), ((uint32_t)(lt / PB) & 1u) ^ 1u)) { ok = false; break; }
       const int64_t tok = (tile_beg + lt) * TM + row;
       const bool valid = tok < tok_end;
       float dm[FD];
@@ -370,18 +402,22 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     };
     load_next(0, dzv, inv, rowb, wgt);
     for (int lt = 0; lt < ntile && ok; ++lt) {
-      const int b = lt & 1, s = lt % XS;
+      const int b = lt % DB, s = lt % XS, sa = lt % AS;
       const int64_t tok = (tile_beg + lt) * TM + row;
       const bool valid = tok < tok_end;
       uint4 dzn[8];
       float inv_n = 0.f, rowb_n = 0.f, wgt_n = 0.f;
       load_next(lt + 1, dzn, inv_n, rowb_n, wgt_n);
-      if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt >> 1) & 1u)) { ok = false; break; }
+      if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt / DB) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
+      if (!WAIT_WARP(BAR(B_AF + sa), (uint32_t)(lt / AS) & 1u)) { ok = false; break; }
       if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_GO);
+#ifdef MHC_TCB_TRACE
+      if (lane == 0 && blockIdx.x == 0 && lt < 64) g_tcb_trace3[lt][e] = (long long)tcb_gtimer();
+#endif
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
-      uint8_t *arow = base + L.xs + s * XSTAGE + (2 + half) * CHUNK + row * 128;  // dx_add tile; dx goes back here
+      uint8_t *arow = base + L.as + sa * XSTAGE + half * CHUNK + row * 128;  // dx_add tile; dx goes back here
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         float d1[16];
@@ -418,14 +454,20 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         }
       }
       if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_MID);
+#ifdef MHC_TCB_TRACE
+      if (lane == 0 && blockIdx.x == 0 && lt < 64) g_tcb_trace2[lt][e] = (long long)tcb_gtimer();
+#endif
       tc_fence_before();
       __syncwarp();  // the warp's 32 x 64 dx block is complete in shared memory
-      if (lane == 0) mbar_arrive(BAR(B_DE + b));
+      if (lane == 0) {
+        mbar_arrive(BAR(B_DE + b));
+        mbar_arrive(BAR(B_XE + s));  // the x tile was read by the arithmetic above
+      }
       // coalesced write-back of the warp's own block: an instruction stores
       // 4 whole 128-byte row segments (lane -> row k*4 + lane/8, granule lane%8)
       {
         const int gq = lane & 7;
-        const uint8_t *blk = base + L.xs + s * XSTAGE + (2 + half) * CHUNK;
+        const uint8_t *blk = base + L.as + sa * XSTAGE + half * CHUNK;
         __nv_bfloat16 *dxb = a.dx + col0 + half * 64 + gq * 8;
         uint4 v[8];
 #pragma unroll
@@ -442,7 +484,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         // the loads above have returned (the stores consumed them): only now
         // may the producer refill the stage
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(B_XE + s));
+        if (lane == 0) mbar_arrive(BAR(B_AE + sa));
         if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_END);
         if (lane == 0) TCB_TRACE(lt, 8 + e);
       }
@@ -462,7 +504,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
 #pragma unroll
         for (int c16 = 0; c16 < NB2 / 16; ++c16) {
           float t16[16];
-          tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + 256u + (uint32_t)c16 * 16u, t16);
+          tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)D2COL + (uint32_t)c16 * 16u, t16);
 #pragma unroll
           for (int i = 0; i < 16; ++i) d2[c16 * 16 + i] = t16[i];
         }
@@ -498,12 +540,10 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-constexpr size_t SMEM_LIMIT = 232448;
-
 template <int N, int MODE>
 static cudaError_t launch_impl(const void *x, BArgs a, int sms, cudaStream_t stream) {
   using Cf = BCfg<N, MODE>;
-  const BLayout L = make_blayout(Cf::K1, Cf::NB2);
+  const BLayout L = make_blayout(Cf::K1, Cf::NB2, Cf::PB);
   const size_t smem = (size_t)L.total + 1024;
   if (smem > SMEM_LIMIT) return cudaErrorNotSupported;
   auto kern = pre_bwd_tc_kernel<N, MODE>;
