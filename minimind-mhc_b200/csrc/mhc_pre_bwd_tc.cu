@@ -418,10 +418,19 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
       uint8_t *arow = base + L.as + sa * XSTAGE + half * CHUNK + row * 128;  // dx_add tile; dx goes back here
+      // 32 accumulator columns per TMEM load (one wait each), used by two
+      // 16-column groups
+      uint32_t d1r[32];
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
+        if ((g & 1) == 0) {
+          tmem_ld32_nowait(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * 128u + (uint32_t)(half * 64 + g * 16),
+                           d1r);
+          tmem_wait_ld();
+        }
         float d1[16];
-        tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)b * 128u + (uint32_t)(half * 64 + g * 16), d1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d1[i] = __uint_as_float(d1r[(g & 1) * 16 + i]);
         if (valid) {
           uint32_t o[8];
 #pragma unroll
