@@ -272,6 +272,18 @@ int mhc_last_path(void);
 int mhc_device_error(int clear);
 
 /*
+ * Self-test of the bounded wait every fused kernel uses: a one-block kernel
+ * waits on an mbarrier that nothing arrives at, with a limit of limit_cycles
+ * SM clock cycles (use_abort != 0: a second warp raises the kernel's abort
+ * flag after ~2e5 cycles, which must end the wait early).  result[0] = 1 if
+ * the wait gave up, result[1] = cycles it lasted.  The kernel then exits
+ * normally and the context stays usable.  Synchronises the device; allocates
+ * 16 bytes of device memory for the result.  limit_cycles in (0, 4e9].  No
+ * reference counterpart (the reference has no device-side waits).
+ */
+int mhc_selftest_bounded_wait(long long limit_cycles, int use_abort, long long *result);
+
+/*
  * mhc_pre_fwd without a caller workspace: the same arguments and results as
  * mhc_pre_fwd minus (workspace, workspace_bytes).  Scratch is a fixed 16 MiB
  * device array inside the library (a file-scope __device__ variable; its

@@ -64,17 +64,24 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   return ok != 0;
 }
 
-// Bounded wait.  Returns false on timeout or when *abort (if given) becomes
-// non-zero.
+// Bounded wait.  Returns false after `limit` clock cycles or as soon as
+// *abort (if given) becomes non-zero.
 template <bool CLUSTER>
-__device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, const volatile int *abort) {
+__device__ __forceinline__ bool wait_parity_limit(uint32_t bar, uint32_t parity, const volatile int *abort,
+                                                  long long limit) {
   const long long t0 = clock64();
   while (true) {
     const bool ok = CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
     if (ok) return true;
     if (abort != nullptr && *abort) return false;
-    if (clock64() - t0 > MHC_WAIT_CYCLES) return false;
+    if (clock64() - t0 > limit) return false;
   }
+}
+
+// The wait every kernel uses: bounded by MHC_WAIT_CYCLES (about one second).
+template <bool CLUSTER>
+__device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, const volatile int *abort) {
+  return wait_parity_limit<CLUSTER>(bar, parity, abort, MHC_WAIT_CYCLES);
 }
 
 // ---- cluster ----------------------------------------------------------------

@@ -53,6 +53,7 @@ _PROTOS = {
     "mhc_set_path_policy": (_I, [_I]),
     "mhc_last_path": (_I, []),
     "mhc_device_error": (_I, [_I]),
+    "mhc_selftest_bounded_wait": (_I, [ctypes.c_longlong, _I, _P]),
     "mhc_pre_fwd_noalloc": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
                                  _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P]),
 }
