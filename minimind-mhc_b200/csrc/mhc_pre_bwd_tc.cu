@@ -310,29 +310,35 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     // ---------------- prep warps: thread = token row of the tile ----------------
     const int row = tid - W_PREP * 32;
     bool ok = true;
-    for (int lt = 0; lt < ntile && ok; ++lt) {
-      const int b = lt % PB;
-      if (!WAIT_WARP(BAR(B_PE + b), ((uint32_t)(lt / PB) & 1u) ^ 1u)) { ok = false; break; }
-      const int64_t tok = (tile_beg + lt) * TM + row;
-      const bool valid = tok < tok_end;
-      float dm[FD];
-      float inv = 0.f;
+    // dm and 1/rms of the next tile are loaded while this tile's operands are
+    // built (the buffer wait would otherwise expose the load latency)
+    auto load_dm = [&](int lt_, float (&dst)[FD], float &inv_) {
+      const int64_t tk = (tile_beg + lt_) * TM + row;
 #pragma unroll
-      for (int j = 0; j < FD; ++j) dm[j] = 0.f;
-      if (valid) {
-        inv = a.inv_rms[tok];
+      for (int j = 0; j < FD; ++j) dst[j] = 0.f;
+      inv_ = 0.f;
+      if (lt_ < ntile && tk < tok_end) {
+        inv_ = a.inv_rms[tk];
         if constexpr (FD % 4 == 0) {
-          const float4 *src = reinterpret_cast<const float4 *>(a.dm + tok * FD);
+          const float4 *src = reinterpret_cast<const float4 *>(a.dm + tk * FD);
 #pragma unroll
           for (int q = 0; q < FD / 4; ++q) {
             const float4 v = src[q];
-            dm[4 * q] = v.x; dm[4 * q + 1] = v.y; dm[4 * q + 2] = v.z; dm[4 * q + 3] = v.w;
+            dst[4 * q] = v.x; dst[4 * q + 1] = v.y; dst[4 * q + 2] = v.z; dst[4 * q + 3] = v.w;
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < FD; ++j) dm[j] = a.dm[tok * FD + j];
+          for (int j = 0; j < FD; ++j) dst[j] = a.dm[tk * FD + j];
         }
       }
+    };
+    float dm[FD], inv;
+    load_dm(0, dm, inv);
+    for (int lt = 0; lt < ntile && ok; ++lt) {
+      const int b = lt % PB;
+      float dmn[FD], invn;
+      load_dm(lt + 1, dmn, invn);
+      if (!WAIT_WARP(BAR(B_PE + b), ((uint32_t)(lt / PB) & 1u) ^ 1u)) { ok = false; break; }
       // A of the dx product: row `row` = [dm_hi | dm_lo | dm_hi | 0], 16-byte granules
       uint8_t *a1 = base + L.a1 + (uint32_t)b * (TM / 8) * a1_sbo(K1);
 #pragma unroll
@@ -376,6 +382,9 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(B_PF + b));
       if (warp == W_PREP && lane == 0) TCB_TRACE(lt, E_PREP_DONE);
+#pragma unroll
+      for (int j = 0; j < FD; ++j) dm[j] = dmn[j];
+      inv = invn;
     }
     if (!ok) record_error(ERR_PREP, abort_flag);
   } else {
