@@ -112,6 +112,9 @@ SHAPES = [
     (16, 8, 12, torch.float32, True),
     (16, 16, 20, torch.float32, False),
     (4, 256, 300, torch.bfloat16, True),
+    (4, 768, 257, torch.bfloat16, True),   # config-2 width: fused forward + tensor-core backward
+    (4, 1024, 130, torch.bfloat16, False),  # config-3 width
+    (2, 512, 129, torch.float16, True),
 ]
 
 
