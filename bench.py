@@ -631,6 +631,32 @@ def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=
     return m
 
 
+def allreduce_grads(params, world):
+    """Average the gradients of `params` over the ranks: one flat bucket per
+    parameter dtype (the fp32 mHC parameters, the bf16 rest), one NCCL
+    all_reduce each.  Every rank reduces every parameter in the same order; a
+    parameter that got no gradient on this rank (an expert no token was routed
+    to) counts as zeros and receives the average, so the buckets, and the
+    collective sequence, are identical on all ranks."""
+    import torch.distributed as dist
+
+    for dt in (torch.float32, torch.bfloat16):
+        ps = [p for p in params if p.dtype == dt]
+        if not ps:
+            continue
+        flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in ps])
+        dist.all_reduce(flat)
+        flat.div_(world)
+        off = 0
+        for p in ps:
+            g = flat[off:off + p.numel()].view_as(p)
+            if p.grad is None:
+                p.grad = g.clone()
+            else:
+                p.grad.copy_(g)
+            off += p.numel()
+
+
 def run_model(args, rank, world, local_rank):
     """configs[3] (--workload c4): forward of the 8-layer decoder, 32 x 2048
     tokens per GPU.  configs[4] (--workload c5): training step (forward,
@@ -665,18 +691,7 @@ def run_model(args, rank, world, local_rank):
         loss = F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), labels.view(-1))
         loss.backward()
         if world > 1:
-            # one flat bucket per dtype: the mHC (fp32) and the rest (bf16)
-            for dt in (torch.float32, torch.bfloat16):
-                gs = [p.grad for p in params if p.grad is not None and p.grad.dtype == dt]
-                if not gs:
-                    continue
-                flat = torch.cat([g.reshape(-1) for g in gs])
-                dist.all_reduce(flat)
-                flat.div_(world)
-                off = 0
-                for g in gs:
-                    g.copy_(flat[off:off + g.numel()].view_as(g))
-                    off += g.numel()
+            allreduce_grads(params, world)
         opt.step()
         opt.zero_grad(set_to_none=True)
 

@@ -113,3 +113,48 @@ def test_allreduced_grads_equal_full_batch_grads(sharded):
 
 def test_step_time_is_max_over_ranks(sharded):
     assert all(sharded[r][2] == float(WORLD) for r in range(WORLD))
+
+
+def _grad_worker(rank, port, q):
+    """bench.py's gradient all-reduce with a parameter that got no gradient on
+    one rank (an MoE expert no token of that rank was routed to)."""
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        ps = [torch.nn.Parameter(torch.zeros(5)), torch.nn.Parameter(torch.zeros(3, 2, dtype=torch.bfloat16)),
+              torch.nn.Parameter(torch.zeros(4, dtype=torch.bfloat16))]
+        ps[0].grad = torch.full((5,), 1.0 + rank)
+        ps[1].grad = torch.full((3, 2), 2.0 * (rank + 1), dtype=torch.bfloat16)
+        if rank == 0:
+            ps[2].grad = torch.full((4,), 6.0, dtype=torch.bfloat16)  # rank 1 leaves this one None
+        bench.allreduce_grads(ps, WORLD)
+        t = torch.tensor([1.0])
+        dist.all_reduce(t)  # the collective sequence is still aligned
+        q.put((rank, [p.grad.float().numpy().copy() for p in ps], t.item()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_allreduce_with_a_missing_gradient():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grad_worker, args=(r, port, q)) for r in range(WORLD)]
+    for pr in procs:
+        pr.start()
+    res = {}
+    for _ in range(WORLD):
+        r, gs, tsum = q.get(timeout=300)
+        res[r] = (gs, tsum)
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    for r in range(WORLD):
+        gs, tsum = res[r]
+        assert tsum == float(WORLD)
+        assert torch.allclose(torch.from_numpy(gs[0]), torch.full((5,), 1.5))
+        assert torch.allclose(torch.from_numpy(gs[1]), torch.full((3, 2), 3.0))
+        assert torch.allclose(torch.from_numpy(gs[2]), torch.full((4,), 3.0))  # (6 + 0) / 2
