@@ -266,29 +266,50 @@ int mhc_last_path(void);
  * 1..6 = a bounded wait of the producer / MMA / row / coefficient /
  * pre-aggregate / Sinkhorn role of the forward kernel ran out, 11..14 = one of
  * the producer / MMA / epilogue / prep roles of the backward tensor-core
- * kernel; the kernel gave up instead of hanging and its outputs are invalid).  Synchronises the device.  clear != 0
- * resets the word.  No reference counterpart.
+ * kernel, 99 = the self-test below).  A kernel whose wait runs out gives up
+ * instead of hanging and overwrites the outputs it owns with NaN.
+ * Synchronises the device.  clear != 0 resets the word.  No reference
+ * counterpart.
  */
 int mhc_device_error(int clear);
+
+/*
+ * Registers a pinned host int (cudaHostAlloc / cudaMallocHost / a pinned
+ * torch tensor; pageable memory is rejected with MHC_ERR_UNSUPPORTED) that
+ * every fused kernel whose bounded wait runs out also writes its error code
+ * into (first code wins).  The host reads it without any synchronisation, so
+ * a caller can check for a give-up on every call at no cost; the code shows
+ * up once the failing kernel has run, i.e. at a later call.  The caller owns
+ * the word and resets it to 0.  NULL unregisters.  Process-wide.  No
+ * reference counterpart.
+ */
+int mhc_set_error_flag(int *host_flag);
 
 /*
  * Self-test of the bounded wait every fused kernel uses: a one-block kernel
  * waits on an mbarrier that nothing arrives at, with a limit of limit_cycles
  * SM clock cycles (use_abort != 0: a second warp raises the kernel's abort
  * flag after ~2e5 cycles, which must end the wait early).  result[0] = 1 if
- * the wait gave up, result[1] = cycles it lasted.  The kernel then exits
- * normally and the context stays usable.  Synchronises the device; allocates
- * 16 bytes of device memory for the result.  limit_cycles in (0, 4e9].  No
- * reference counterpart (the reference has no device-side waits).
+ * the wait gave up, result[1] = cycles it lasted.  On giving up the kernel
+ * takes the fused kernels' give-up path: error code 99 in its device word
+ * (mhc_device_error) and in the registered host flag (mhc_set_error_flag),
+ * and NaN over poison[0 .. poison_n) (a device fp32 buffer, or NULL with
+ * poison_n = 0).  The kernel then exits normally and the context stays
+ * usable.  Synchronises the device; allocates 16 bytes of device memory for
+ * the result.  limit_cycles in (0, 4e9].  No reference counterpart (the
+ * reference has no device-side waits).
  */
-int mhc_selftest_bounded_wait(long long limit_cycles, int use_abort, long long *result);
+int mhc_selftest_bounded_wait(long long limit_cycles, int use_abort, long long *result, float *poison,
+                              long long poison_n);
 
 /*
  * mhc_pre_fwd without a caller workspace: the same arguments and results as
  * mhc_pre_fwd minus (workspace, workspace_bytes).  Scratch is a fixed 16 MiB
  * device array inside the library (a file-scope __device__ variable; its
  * address is looked up once per device, on the first call on that device --
- * make that first call outside any stream capture).  Limit: T*n <= 4,194,304;
+ * make that first call outside any stream capture; the looked-up address is not
+ * valid after cudaDeviceReset of that device, so do not use this entry point
+ * in a process after such a reset).  Limit: T*n <= 4,194,304;
  * larger batches are rejected with MHC_ERR_WORKSPACE before any CUDA call.
  * Nothing is allocated and nothing in the scratch needs to start at zero.
  * All calls on one device share the scratch: two calls that overlap in time

@@ -1,6 +1,7 @@
 // C ABI entry points (include/mhc_b200.h): argument validation, workspace
 // carving and dispatch to the kernel launchers.  No entry point allocates,
 // synchronises or launches anything when its arguments are rejected.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -55,6 +56,11 @@ static int check_shape(int64_t T, int n, int C) {
 static int g_policy = MHC_PATH_AUTO;
 static thread_local int g_last_path = 0;
 
+// Pinned host word the fused kernels also write their give-up code into
+// (mhc_set_error_flag); null until a caller registers one.
+static std::atomic<int *> g_host_flag{nullptr};
+int *host_error_flag() { return g_host_flag.load(std::memory_order_acquire); }
+
 static int check_elem_align(const void *p, int dtype, const char *name) {
   if (p && !aligned(p, esize(dtype))) return fail(MHC_ERR_ALIGN, "%s is not %zu-byte aligned", name, esize(dtype));
   return MHC_OK;
@@ -90,8 +96,29 @@ int mhc_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
   const int fwd = read_tc_error(clear != 0);
   const int bwd = read_tcb_error(clear != 0);
-  if (fwd < 0 || bwd < 0) return -1;
-  return fwd != 0 ? fwd : bwd;
+  const int st = read_selftest_error(clear != 0);
+  if (fwd < 0 || bwd < 0 || st < 0) return -1;
+  return fwd != 0 ? fwd : (bwd != 0 ? bwd : st);
+}
+
+int mhc_set_error_flag(int *host_flag) {
+  g_err[0] = 0;
+  if (host_flag) {
+    if (!aligned(host_flag, 4)) return fail(MHC_ERR_ALIGN, "mhc_set_error_flag: flag is not 4-byte aligned");
+    cudaPointerAttributes at;
+    const cudaError_t e = cudaPointerGetAttributes(&at, host_flag);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_status(e, "mhc_set_error_flag: cudaPointerGetAttributes");
+    }
+    // pinned (page-locked) host memory is addressable by every device at the
+    // same pointer under unified addressing; pageable memory is not
+    if (at.type != cudaMemoryTypeHost || at.devicePointer != static_cast<void *>(host_flag))
+      return fail(MHC_ERR_UNSUPPORTED, "mhc_set_error_flag: the flag must be pinned host memory "
+                                       "(cudaHostAlloc / cudaMallocHost / torch pin_memory)");
+  }
+  g_host_flag.store(host_flag, std::memory_order_release);
+  return MHC_OK;
 }
 
 size_t mhc_pre_fwd_workspace(int64_t T, int n, int C, int with_res) {
@@ -393,7 +420,10 @@ static std::mutex g_noalloc_mu;
 static void *g_noalloc_ptr[128] = {nullptr};
 
 // Device address of the scratch on the current device, looked up once per
-// device (the first call on a device does the lookup).
+// device (the first call on a device does the lookup).  The cached address
+// belongs to the device's current context: after cudaDeviceReset the module is
+// loaded again and the array may sit elsewhere, so the entry point must not be
+// used in a process after such a reset.
 static int noalloc_scratch(void **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -85,6 +85,12 @@ cudaError_t launch_pre_bwd_tc(int mode, int n, const void *x, int64_t T, int C, 
                               cudaStream_t stream);
 int read_tcb_error(bool clear);
 
+// Pinned host word registered with mhc_set_error_flag (null when none): the
+// fused kernels' give-up path writes its error code there as well as into
+// their device error words.
+int *host_error_flag();
+int read_selftest_error(bool clear);
+
 // ---- stand-alone pieces -----------------------------------------------------
 cudaError_t launch_sinkhorn_fwd(int n, const void *M, int m_dtype, void *Y, int y_dtype,
                                 int64_t batch, int iters, float eps, cudaStream_t stream);

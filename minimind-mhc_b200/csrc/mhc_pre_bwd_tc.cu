@@ -85,24 +85,6 @@ struct BCfg {
   static_assert(NB2 <= TMEM_COLS - D2COL, "dphi accumulator must fit after the dx accumulators");
 };
 
-// Per-tile timeline instrumentation (global timer, block 0), compiled in only
-// with -DMHC_TCB_TRACE; events are indexed [local tile][event].
-#ifdef MHC_TCB_TRACE
-__device__ long long g_tcb_trace[64][16];
-__device__ long long g_tcb_trace2[64][8];
-__device__ long long g_tcb_trace3[64][8];
-__device__ unsigned long long g_tcb_t0 = ~0ull;
-__device__ __forceinline__ unsigned long long tcb_gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-#define TCB_TRACE(lt_, ev) do { if (blockIdx.x == 0 && (lt_) < 64) g_tcb_trace[lt_][ev] = (long long)tcb_gtimer(); } while (0)
-#else
-#define TCB_TRACE(lt_, ev) do { } while (0)
-#endif
-enum TcbEv { E_P_ISSUE, E_M_PF, E_M_XF, E_M_GO, E_PREP_DONE, E_EPI_GO, E_EPI_END, E_EPI_MID, E_EPI_LAST };
-
 // barrier slots
 constexpr int B_XF = 0, B_XE = XS, B_AF = 2 * XS, B_AE = B_AF + AS, B_PF = B_AE + AS, B_PE = B_PF + 2,
               B_DF = B_PE + 2, B_DE = B_DF + DB, B_DRAIN = B_DE + DB, NBARS = B_DRAIN + 1;
@@ -135,6 +117,7 @@ struct BArgs {
   const __nv_bfloat16 *dz, *dx_add;
   __nv_bfloat16 *dx;
   float *dphi_part;  // [TS][nC][FD]
+  int *err_flag;     // pinned host error word (mhc_set_error_flag) or null
 };
 
 // byte offset of (row r, column k) of a no-swizzle K-major operand built from
@@ -150,9 +133,9 @@ __device__ __forceinline__ uint32_t mn_off(int n, int k, uint32_t sbo) {
   return (uint32_t)(n >> 3) * sbo + (uint32_t)(k >> 3) * 128u + (uint32_t)(k & 7) * 16u + (uint32_t)(n & 7) * 2u;
 }
 
-__device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
+__device__ __forceinline__ void record_error(int code, volatile int *abort_flag, int *err_flag) {
   *abort_flag = 1;
-  atomicCAS(&g_tcb_error, 0, code);
+  report_give_up(&g_tcb_error, err_flag, code);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -231,9 +214,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
   }
   fence_proxy_async_smem();
   __syncthreads();
-#ifdef MHC_TCB_TRACE
-  if (threadIdx.x == 0) atomicMin(&g_tcb_t0, tcb_gtimer());
-#endif
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base + L.tmem);
 
   if (warp == W_PROD || warp == W_APROD) {
@@ -251,7 +231,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       for (; lt < ntile && ok; ++lt) {
         const int s = lt % NS;
         if (!wait_parity<false>(BAR(be + s), ((uint32_t)(lt / NS) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-        if (is_x) TCB_TRACE(lt, E_P_ISSUE);
         if (!load) {
           mbar_arrive(BAR(bf + s));  // no dx_add: the buffer only receives dx
           continue;
@@ -261,7 +240,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         tma_load_2d(ring + s * XSTAGE, map, col0, t0, BAR(bf + s));
         tma_load_2d(ring + s * XSTAGE + CHUNK, map, col0 + 64, t0, BAR(bf + s));
       }
-      if (!ok) record_error(ERR_PROD, abort_flag);
+      if (!ok) record_error(ERR_PROD, abort_flag, a.err_flag);
       const int l0 = lt > NS ? lt - NS : 0;
       for (int p = l0; p < lt; ++p) wait_parity<false>(BAR(bf + p % NS), (uint32_t)(p / NS) & 1u, nullptr);
     }
@@ -276,11 +255,8 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         const int b = lt % DB, s = lt % XS, pb = lt % PB;
         const uint32_t bph = (uint32_t)(lt / DB) & 1u;
         if (!wait_parity<false>(BAR(B_PF + pb), (uint32_t)(lt / PB) & 1u, abort_flag)) { ok = false; break; }
-        TCB_TRACE(lt, E_M_PF);
         if (!wait_parity<false>(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u, abort_flag)) { ok = false; break; }
-        TCB_TRACE(lt, E_M_XF);
         if (!wait_parity<false>(BAR(B_DE + b), bph ^ 1u, abort_flag)) { ok = false; break; }
-        TCB_TRACE(lt, E_M_GO);
         tc_fence_after();
         // dx product into D1[b]
         const uint32_t a1 = base_u32 + L.a1 + (uint32_t)pb * (TM / 8) * a1_sbo(K1);
@@ -302,7 +278,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         umma_commit(BAR(B_PE + pb));
         umma_commit(BAR(B_XE + s));
       }
-      if (!ok) record_error(ERR_MMA, abort_flag);
+      if (!ok) record_error(ERR_MMA, abort_flag, a.err_flag);
       umma_commit(BAR(B_DRAIN));
     }
     __syncwarp();
@@ -381,12 +357,11 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       fence_proxy_async_smem();  // generic writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(B_PF + b));
-      if (warp == W_PREP && lane == 0) TCB_TRACE(lt, E_PREP_DONE);
 #pragma unroll
       for (int j = 0; j < FD; ++j) dm[j] = dmn[j];
       inv = invn;
     }
-    if (!ok) record_error(ERR_PREP, abort_flag);
+    if (!ok) record_error(ERR_PREP, abort_flag, a.err_flag);
   } else {
     // ---------------- dx epilogue ----------------
     const int e = warp - W_EPI;
@@ -420,10 +395,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       if (!WAIT_WARP(BAR(B_DF + b), (uint32_t)(lt / DB) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_XF + s), (uint32_t)(lt / XS) & 1u)) { ok = false; break; }
       if (!WAIT_WARP(BAR(B_AF + sa), (uint32_t)(lt / AS) & 1u)) { ok = false; break; }
-      if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_GO);
-#ifdef MHC_TCB_TRACE
-      if (lane == 0 && blockIdx.x == 0 && lt < 64) g_tcb_trace3[lt][e] = (long long)tcb_gtimer();
-#endif
       tc_fence_after();
       const uint8_t *xrow = base + L.xs + s * XSTAGE + half * CHUNK + row * 128;
       uint8_t *arow = base + L.as + sa * XSTAGE + half * CHUNK + row * 128;  // dx_add tile; dx goes back here
@@ -471,10 +442,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
           }
         }
       }
-      if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_MID);
-#ifdef MHC_TCB_TRACE
-      if (lane == 0 && blockIdx.x == 0 && lt < 64) g_tcb_trace2[lt][e] = (long long)tcb_gtimer();
-#endif
       tc_fence_before();
       __syncwarp();  // the warp's 32 x 64 dx block is complete in shared memory
       if (lane == 0) {
@@ -503,8 +470,6 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
         // may the producer refill the stage
         __syncwarp();
         if (lane == 0) mbar_arrive(BAR(B_AE + sa));
-        if (warp == W_EPI && lane == 0) TCB_TRACE(lt, E_EPI_END);
-        if (lane == 0) TCB_TRACE(lt, 8 + e);
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) dzv[q] = dzn[q];
@@ -512,7 +477,7 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
       rowb = rowb_n;
       wgt = wgt_n;
     }
-    if (!ok) record_error(ERR_EPI, abort_flag);
+    if (!ok) record_error(ERR_EPI, abort_flag, a.err_flag);
     // dphi partial of this CTA: D2 lanes are its columns
     if (half == 0) {
       const bool drained = WAIT_WARP(BAR(B_DRAIN), 0u);
@@ -540,6 +505,19 @@ pre_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constan
     wait_parity<false>(BAR(B_DRAIN), 0u, nullptr);
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (*abort_flag) {
+    // a wait gave up: the CTA's whole share (dx of its 128 columns over its
+    // token range, its dphi partial) becomes NaN instead of partly written
+    const float qnan = __int_as_float(0x7fc00000);
+    const __nv_bfloat16 bnan = __float2bfloat16_rn(qnan);
+    const int64_t t_beg = tile_beg * TM;
+    for (int64_t e = tid; e < (tok_end - t_beg) * KCOL; e += NTHREADS) {
+      const int64_t r = e / KCOL;
+      a.dx[(t_beg + r) * a.nC + col0 + (int)(e - r * KCOL)] = bnan;
+    }
+    float *dst = a.dphi_part + ((int64_t)split * a.nC + col0) * FD;
+    for (int e = tid; e < KCOL * FD; e += NTHREADS) dst[e] = qnan;
   }
 #undef WAIT_WARP
 #undef BAR
@@ -653,6 +631,7 @@ cudaError_t launch_pre_bwd_tc(int mode, int n, const void *x, int64_t T, int C, 
   a.dx_add = reinterpret_cast<const __nv_bfloat16 *>(dx_add);
   a.dx = reinterpret_cast<__nv_bfloat16 *>(dx);
   a.dphi_part = dphi_part;
+  a.err_flag = host_error_flag();
   const int sms = device_sm_count();
   return with_mode(mode, [&](auto md) -> cudaError_t {
     constexpr int MODE = decltype(md)::value;

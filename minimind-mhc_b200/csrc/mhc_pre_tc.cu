@@ -92,32 +92,6 @@ static_assert(Z_LAG <= HB, "the producer's ZD wait must not skip a phase");
 // block x . x^T of the chunk rows (128 columns) after it; two buffers.
 constexpr int ACC_STRIDE = 256, TMEM_COLS = 512;
 
-// Per-tile timeline instrumentation (global timer, cluster 0 / CTA 0), compiled in
-// only with -DMHC_TC_TRACE; events are indexed [local tile][event].
-#ifdef MHC_TC_TRACE
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ long long g_trace[64][32];
-#define TC_TRACE(ev) do { if (cid == 0 && rank == 0 && lt < 64) g_trace[lt][ev] = (long long)gtimer(); } while (0)
-__device__ long long g_trace_ch[64][8][8];
-#define TC_TRACE_CH(c, k) do { if (cid == 0 && rank == 0 && lt < 64 && (c) < 8) g_trace_ch[lt][c][k] = (long long)gtimer(); } while (0)
-// global-timer (ns) marks: [0] min kernel entry, [1] max end of prologue, [2] max loop end, [3] max exit
-__device__ unsigned long long g_trace_ns[4] = {~0ull, 0, 0, 0};
-__device__ unsigned long long g_trace_cta[256][2];  // per CTA: loop start, loop end
-#define TC_MARK(i) do { if (threadIdx.x == 0) { const unsigned long long now_ = gtimer(); \
-  if ((i) == 0) atomicMin(&g_trace_ns[0], now_); else atomicMax(&g_trace_ns[i], now_); \
-  if ((i) == 1 || (i) == 2) g_trace_cta[blockIdx.x & 255][(i) - 1] = now_; } } while (0)
-#else
-#define TC_MARK(i) do { } while (0)
-#define TC_TRACE(ev) do { } while (0)
-#define TC_TRACE_CH(c, k) do { } while (0)
-#endif
-enum TraceEv { T_P_FIRST, T_P_LAST, T_M_ACCE, T_M_COMMIT, T_R_FULL0, T_R_ACCF, T_R_INE, T_R_PUSHED, T_C_INF,
-               T_C_HPE, T_C_PUSHED, T_Z_BOX3, T_Z_HPF, T_SK_LGF, T_SK_DONE, T_Z_BOX0, T_Z_DONE, T_ZP_GO, T_C_LGE };
-
 enum ErrCode { ERR_PROD = 1, ERR_MMA = 2, ERR_ROW = 3, ERR_COEF = 4, ERR_Z = 5, ERR_SK = 6 };
 
 template <int N, int MODE>
@@ -178,6 +152,7 @@ struct Args {
   void *h_pre, *h_post, *h_res;
   int coef_dtype;
   float *inv_rms, *mixes;
+  int *err_flag;        // pinned host error word (mhc_set_error_flag) or null
 };
 
 // byte offset of element (row j, column kk < 64) inside one phi chunk block:
@@ -186,9 +161,45 @@ __device__ __forceinline__ uint32_t phi_off(int j, int kk, int NB) {
   return (uint32_t)(j >> 3) * 1024 + (j & 7) * 128 + ((((kk >> 3) ^ (j & 7))) << 4) + ((kk & 7) << 1);
 }
 
-__device__ __forceinline__ void record_error(int code, volatile int *abort_flag) {
+__device__ __forceinline__ void record_error(int code, volatile int *abort_flag, int *err_flag) {
   *abort_flag = 1;
-  atomicCAS(&g_tc_error, 0, code);
+  report_give_up(&g_tc_error, err_flag, code);
+}
+
+// After a wait gave up, the CTA overwrites its share of every tile of its
+// cluster with NaN: z columns [c0, c0 + C/S) of the tile's rows and every
+// per-token output of its TPC tokens.  A consumer of partly written outputs
+// therefore sees NaN rather than plausible numbers.
+template <int N, int MODE>
+__device__ void poison_share(const Args &a, int cid, int ncl, int rank, int ntiles, int tid, int nthreads) {
+  constexpr int FD = Dims<N, MODE>::FD;
+  const float qnan = __int_as_float(0x7fc00000);
+  const __nv_bfloat16 bnan = __float2bfloat16_rn(qnan);
+  const int cz = a.C / S, c0 = rank * cz;
+  for (int tile = cid; tile < ntiles; tile += ncl) {
+    const int64_t t0 = (int64_t)tile * TM;
+    const int rows = a.T - t0 < TM ? (int)(a.T - t0) : TM;
+    for (int e = tid; e < rows * cz; e += nthreads) {
+      const int r = e / cz, c = e - r * cz;
+      a.z[(t0 + r) * a.C + c0 + c] = bnan;
+    }
+    for (int e = tid; e < TPC; e += nthreads) {
+      const int64_t tok = t0 + rank * TPC + e;
+      if (tok >= a.T) continue;
+      a.inv_rms[tok] = qnan;
+      for (int j = 0; j < FD; ++j) a.mixes[tok * FD + j] = qnan;
+      if constexpr (MODE != HEAD) {
+        for (int i = 0; i < N; ++i) {
+          if (a.h_pre) store_dyn(a.h_pre, a.coef_dtype, tok * N + i, qnan);
+          store_dyn(a.h_post, a.coef_dtype, tok * N + i, qnan);
+        }
+      }
+      if constexpr (MODE == FULL) {
+        if (a.h_res)
+          for (int k = 0; k < N * N; ++k) store_dyn(a.h_res, a.coef_dtype, tok * N * N + k, qnan);
+      }
+    }
+  }
 }
 
 template <int N, int MODE>
@@ -232,7 +243,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
 // agrees on the outcome so it always leaves a loop together
 #define WAIT_WARP(CL, bar, par) (__all_sync(0xffffffffu, wait_parity<CL>((bar), (par), abort_flag)))
 
-  TC_MARK(0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_ctarank(), cid = cluster_id_x(), ncl = ncluster_x();
   const int ntiles = (int)((a.T + TM - 1) / TM);
@@ -358,7 +368,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
     __syncwarp();
     if (lane == 0) mbar_arrive(BAR(B_PHI));
   }
-  TC_MARK(1);
 
   if (warp == W_PROD) {
     if (lane == 0) {
@@ -378,15 +387,12 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
-          TC_TRACE_CH(c, 0);
-          if (c == 0) TC_TRACE(T_P_FIRST);
-          if (c == CH - 1) TC_TRACE(T_P_LAST);
           mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
           tma_load_2d_hint(base_u32 + L.ring + slot * SLOT + XOFF, &tmap, (int)rank * a.KS + c * 64, tile * TM,
                            BAR(B_FULL + slot), keep);
         }
       }
-      if (!ok) record_error(ERR_PROD, abort_flag);
+      if (!ok) record_error(ERR_PROD, abort_flag, a.err_flag);
       // copies in flight must land before the CTA can exit
       const uint32_t q0 = q > (uint32_t)RING ? q - RING : 0u;
       for (uint32_t p = q0; p < q; ++p) wait_parity<false>(BAR(B_FULL + p % RING), (p / RING) & 1u, nullptr);
@@ -405,13 +411,11 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         const int buf = lt & 1;
         const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
         if (!wait_parity<false>(BAR(B_ACCE + buf), aph ^ 1u, abort_flag)) { ok = false; break; }
-        TC_TRACE(T_M_ACCE);
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)buf * ACC_STRIDE;
         for (int c = 0; c < CH; ++c, ++q) {
           const uint32_t slot = q % RING, ph = (q / RING) & 1u;
           if (!wait_parity<false>(BAR(B_FULL + slot), ph, abort_flag)) { ok = false; break; }
-          TC_TRACE_CH(c, 1);
           tc_fence_after();
           // sum of squares of each row = diagonal of x . x^T: the chunk is
           // (part of) its own B operand (same K-major 128-byte-swizzled rows)
@@ -434,9 +438,8 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         }
         if (!ok) break;
         umma_commit(BAR(B_ACCF + buf));
-        TC_TRACE(T_M_COMMIT);
       }
-      if (!ok) record_error(ERR_MMA, abort_flag);
+      if (!ok) record_error(ERR_MMA, abort_flag, a.err_flag);
       // every issued MMA completes before TMEM is released
       umma_commit(BAR(B_DRAIN));
       wait_parity<false>(BAR(B_DRAIN), 0u, nullptr);
@@ -453,8 +456,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       const int buf = lt & 1;
       const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
       if (!WAIT_WARP(false, BAR(B_ACCF + buf), aph)) { ok = false; break; }
-      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_ACCF);
-      if (lane == 0) TC_TRACE_CH(6, quad);
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * ACC_STRIDE;
       float d[NB];
@@ -486,18 +487,14 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       // the owners' inbox buffer must have been drained (tile lt - IN_BUFS)
       const int ib = lt % IN_BUFS;
       if (!WAIT_WARP(true, BAR(B_INE + ib), ((uint32_t)(lt / IN_BUFS) & 1u) ^ 1u)) { ok = false; break; }
-      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_INE);
-      if (lane == 0) TC_TRACE_CH(7, quad);
       const uint32_t dst = mapa(base_u32 + L.inbox + (uint32_t)(((ib * S + (int)rank) * TPC + (row % TPC)) * IBS * 4),
                                 owner);
       const uint32_t dbar = mapa(BAR(B_INF + ib), owner);
 #pragma unroll
       for (int v = 0; v < IBS / 4; ++v)
         st_async_v4(dst + v * 16, vals[4 * v], vals[4 * v + 1], vals[4 * v + 2], vals[4 * v + 3], dbar);
-      if (warp == W_ROW && lane == 0) TC_TRACE(T_R_PUSHED);
-      if (lane == 0) TC_TRACE_CH(7, 4 + quad);
     }
-    if (!ok) record_error(ERR_ROW, abort_flag);
+    if (!ok) record_error(ERR_ROW, abort_flag, a.err_flag);
   } else if (warp == W_COEF) {
     // ---------------- coefficient warp ----------------
     int lt = 0;
@@ -507,7 +504,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       const uint32_t iph = (uint32_t)(lt / IN_BUFS) & 1u, hph = (uint32_t)(lt / HB) & 1u;
       if (lane == 0) mbar_arrive_expect_tx(BAR(B_INF + ib), INBOX_TX);  // arm: all 8 slices' rows
       if (!WAIT_WARP(true, BAR(B_INF + ib), iph)) { ok = false; break; }
-      if (lane == 0) TC_TRACE(T_C_INF);
       float acc[IBS];
 #pragma unroll
       for (int j = 0; j < IBS; ++j) acc[j] = 0.f;
@@ -533,7 +529,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       for (int i = 0; i < HPN; ++i) w[i] = 0.f;
       // the weights buffer `hb` must be free in every CTA (tile lt-HB done everywhere)
       if (!WAIT_WARP(true, BAR(B_HPE + hb), hph ^ 1u)) { ok = false; break; }
-      if (lane == 0) TC_TRACE(T_C_HPE);
       // every CTA finished this tile's projection, so its x is in L2: start the
       // pre-aggregate loads.  Signalled only after tile lt-HB is done everywhere,
       // so no pre-aggregate warp can see two phases of ZGO[hb] at once.
@@ -542,7 +537,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       const int lb = lt % HBL;
       if constexpr (MODE == FULL) {
         if (!WAIT_WARP(false, BAR(B_LGE + lb), ((uint32_t)(lt / HBL) & 1u) ^ 1u)) { ok = false; break; }
-        if (lane == 0) TC_TRACE(T_C_LGE);
       }
       if (lane < TPC) {
         inv = rsqrtf(acc[FD] / (float)a.nC + a.p.rms_eps);
@@ -570,7 +564,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
             st_async_v4(dst + v * 16, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3], dbar);
         }
       }
-      if (lane == 0) TC_TRACE(T_C_PUSHED);
       if constexpr (MODE == FULL) {
         __syncwarp();
         if (lane == 0) mbar_arrive(BAR(B_LGF + lb));  // logits ready for the Sinkhorn warp
@@ -589,7 +582,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         }
       }
     }
-    if (!ok) record_error(ERR_COEF, abort_flag);
+    if (!ok) record_error(ERR_COEF, abort_flag, a.err_flag);
   } else if (warp == W_SK) {
     // ---------------- Sinkhorn warp: H_res of the CTA's 16 tokens ----------------
     // Lanes 0-15 take the tokens of local tile lt, lanes 16-31 those of tile
@@ -605,7 +598,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
           ok = false;
           break;
         }
-        TC_TRACE(T_SK_LGF);
         const int my_lt = lt + half, hb = my_lt % HBL;
         const int64_t tok = (int64_t)(tile + half * (int)ncl) * TM + (int)rank * TPC + (lane & 15);
         if ((half == 0 || two) && tok < a.T) {
@@ -619,13 +611,12 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
           }
         }
         __syncwarp();
-        TC_TRACE(T_SK_DONE);
         if (lane == 0) {
           mbar_arrive(BAR(B_LGE + lt % HBL));  // logits buffers free
           if (two) mbar_arrive(BAR(B_LGE + (lt + 1) % HBL));
         }
       }
-      if (!ok) record_error(ERR_SK, abort_flag);
+      if (!ok) record_error(ERR_SK, abort_flag, a.err_flag);
     }
   } else {
     // ---------------- pre-aggregate warps ----------------
@@ -649,7 +640,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
       if (warp == W_Z && lane == 0) mbar_arrive_expect_tx(BAR(B_HPF + hb), HP_TX);  // arm: 8 CTAs' weights
       // the tile's x is in L2 once every CTA has finished its projection
       if (!WAIT_WARP(false, BAR(B_ZGO + hb), hph)) { ok = false; break; }
-      if (warp == W_Z && lane == 0) TC_TRACE(T_ZP_GO);
       const int64_t t0 = (int64_t)tile * TM;
       const int rows = a.T - t0 < TM ? (int)(a.T - t0) : TM;
       const __nv_bfloat16 *xb = x + t0 * a.nC + c0;
@@ -674,7 +664,6 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         }
         if (b == 0) {
           if (!WAIT_WARP(true, BAR(B_HPF + hb), hph)) { ok = false; break; }
-          if (warp == W_Z && lane == 0) TC_TRACE(T_Z_HPF);
         }
 #pragma unroll
         for (int u = 0; u < IPB; ++u) {
@@ -715,25 +704,23 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         int good = 1;
         if (lane == 0) {
           good = wait_parity<false>(BAR(B_ZD + hb), hph, abort_flag) ? 1 : 0;
-          TC_TRACE(T_Z_DONE);
           if (good)
             for (int s = 0; s < S; ++s) mbar_arrive_remote(mapa(BAR(B_HPE + hb), (uint32_t)s));
         }
         if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
       }
     }
-    if (!ok) record_error(ERR_Z, abort_flag);
+    if (!ok) record_error(ERR_Z, abort_flag, a.err_flag);
   }
 
   // ---------------- teardown ----------------
   __syncthreads();
-  TC_MARK(2);
   if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+  if (*abort_flag) poison_share<N, MODE>(a, (int)cid, (int)ncl, (int)rank, ntiles, tid, NTHREADS);
   cluster_sync_all();  // no CTA leaves while a peer may still touch its shared memory
-  TC_MARK(3);
 #undef WAIT_WARP
 #undef BAR
 }
@@ -941,6 +928,7 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
   a.coef_dtype = coef_dtype;
   a.inv_rms = inv_rms;
   a.mixes = mixes;
+  a.err_flag = host_error_flag();
   return with_mode(mode, [&](auto md) -> cudaError_t {
     constexpr int MODE = decltype(md)::value;
     switch (n) {

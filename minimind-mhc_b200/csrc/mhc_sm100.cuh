@@ -84,6 +84,19 @@ __device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, const
   return wait_parity_limit<CLUSTER>(bar, parity, abort, MHC_WAIT_CYCLES);
 }
 
+// What a kernel does when one of its bounded waits gives up: the first error
+// code wins in the kernel's device error word and, if the caller registered
+// one (mhc_set_error_flag), in a pinned host word that the host can read
+// without synchronising.  The kernel then poisons (NaN) the outputs it owns
+// and exits normally.
+__device__ __forceinline__ void report_give_up(int *dev_word, int *host_flag, int code) {
+  atomicCAS(dev_word, 0, code);
+  if (host_flag != nullptr) {
+    atomicCAS_system(host_flag, 0, code);
+    __threadfence_system();
+  }
+}
+
 // ---- cluster ----------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

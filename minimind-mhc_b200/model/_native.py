@@ -53,7 +53,8 @@ _PROTOS = {
     "mhc_set_path_policy": (_I, [_I]),
     "mhc_last_path": (_I, []),
     "mhc_device_error": (_I, [_I]),
-    "mhc_selftest_bounded_wait": (_I, [ctypes.c_longlong, _I, _P]),
+    "mhc_set_error_flag": (_I, [_P]),
+    "mhc_selftest_bounded_wait": (_I, [ctypes.c_longlong, _I, _P, _P, ctypes.c_longlong]),
     "mhc_pre_fwd_noalloc": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
                                  _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P]),
 }
@@ -124,5 +125,62 @@ def workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+# ---------------------------------------------------------------------------
+# Device-side give-ups reach the caller
+#
+# Every wait inside the fused kernels is bounded.  A kernel whose wait runs out
+# writes its error code into a pinned host word registered here
+# (mhc_set_error_flag), overwrites the outputs it owns with NaN and exits.
+# Reading the word costs no synchronisation, so every call below checks it and
+# raises once a kernel has given up (the give-up of one call is seen by a later
+# one, as with CUDA's asynchronous errors).  The error stays raised until
+# clear_device_error().
+# ---------------------------------------------------------------------------
+
+ERROR_ROLES = {1: "forward TMA producer", 2: "forward MMA issuer", 3: "forward row warps",
+               4: "forward coefficient warp", 5: "forward pre-aggregate warps", 6: "forward Sinkhorn warp",
+               11: "backward TMA producer", 12: "backward MMA issuer", 13: "backward epilogue",
+               14: "backward prep warps", 99: "bounded-wait self-test"}
+
+_flag_tensor = None   # pinned int32 host tensor registered with the library
+_flag_word = None     # ctypes view of its first element
+
+
+def _register_error_flag():
+    global _flag_tensor, _flag_word
+    with _lock:
+        if _flag_word is not None:
+            return
+        t = torch.zeros(4, dtype=torch.int32).pin_memory()
+        check(lib().mhc_set_error_flag(t.data_ptr()), "mhc_set_error_flag")
+        _flag_tensor = t
+        _flag_word = ctypes.c_int.from_address(t.data_ptr())
+
+
+def device_error_code() -> int:
+    """The first give-up code a fused kernel wrote since the last clear (0 = none)."""
+    return 0 if _flag_word is None else int(_flag_word.value)
+
+
+def raise_if_device_error():
+    code = device_error_code()
+    if code:
+        role = ERROR_ROLES.get(code, "unknown role")
+        raise RuntimeError(
+            f"an mHC kernel gave up on a bounded device wait (code {code}: {role}); the outputs it owned "
+            f"were overwritten with NaN.  Call model._native.clear_device_error() to continue.")
+
+
+def clear_device_error():
+    """Resets the host word and the device error words (synchronises the device)."""
+    if torch.cuda.is_available():
+        lib().mhc_device_error(1)
+    if _flag_word is not None:
+        _flag_word.value = 0
+
+
 def call(name: str, *args):
+    if _flag_word is None:
+        _register_error_flag()
+    raise_if_device_error()
     check(getattr(lib(), name)(*args), name)
