@@ -333,6 +333,13 @@ class _MHCPostFn(torch.autograd.Function):
         return None, dhr, dhp, df.view(b, l, c), None, None, None, None, None, None
 
 
+def raise_no_cpu_path(cls_name: str):
+    raise RuntimeError(
+        f"{cls_name}._forward_ref: this B200 build has no CPU path (all math runs in the sm_100a "
+        f"kernels).  Load the state_dict into the reference module for a CPU run; the parameter "
+        f"names, shapes and dtypes are identical.")
+
+
 def mhc_connection(x_flat, sublayer_fn, phi, alpha_pre, bias_pre, alpha_post, bias_post,
                    alpha_res, bias_res, *, n, c, sinkhorn_iters, post_mult, eps, pre_eps,
                    sinkhorn_eps, with_res=True):
@@ -391,3 +398,10 @@ class MHCConnection_Fused(nn.Module):
                               n=self.n, c=self.dim, sinkhorn_iters=self.sinkhorn_iters,
                               post_mult=self.post_mult_value, eps=self.eps, pre_eps=self.pre_eps,
                               sinkhorn_eps=self.sinkhorn_eps, with_res=True)
+
+    def _forward_ref(self, x_flat: torch.Tensor, sublayer_fn) -> torch.Tensor:
+        """The reference's pure-PyTorch path (``model/mhc_fused.py:836-864``)
+        is not part of this build, which has no CPU path: the name is kept so
+        that callers get this explanation instead of an AttributeError.  For a
+        CPU run, load the same state_dict into the reference module."""
+        raise_no_cpu_path(type(self).__name__)

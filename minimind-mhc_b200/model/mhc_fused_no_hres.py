@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 
 from . import _native as nat
-from .mhc_fused import _contig_or_none, _params, _pre_bwd, _pre_fwd, mhc_connection
+from .mhc_fused import _contig_or_none, _params, _pre_bwd, _pre_fwd, mhc_connection, raise_no_cpu_path
 
 
 def _is_pow2(n: int) -> bool:
@@ -139,3 +139,9 @@ class MHCConnection_FusedNoHres(nn.Module):
                               self.alpha_post, self.bias_post, None, None, n=self.n, c=self.dim,
                               sinkhorn_iters=0, post_mult=self.post_mult_value, eps=self.eps,
                               pre_eps=self.pre_eps, sinkhorn_eps=0.0, with_res=False)
+
+    def _forward_ref(self, x_flat: torch.Tensor, sublayer_fn) -> torch.Tensor:
+        """The reference's pure-PyTorch path (``model/mhc_fused_no_hres.py:635-659``)
+        is not part of this build, which has no CPU path: the name is kept so
+        that callers get this explanation instead of an AttributeError."""
+        raise_no_cpu_path(type(self).__name__)

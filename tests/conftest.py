@@ -22,6 +22,17 @@ def golden():
     return torch.load(GOLDEN_PATH, weights_only=False)
 
 
+def golden_sublayer(g, to=None):
+    """The sublayer function a golden module case was generated with."""
+    import torch.nn.functional as F
+    if g["sub"] == "mlp":
+        w1, w2 = (g["w1"], g["w2"]) if to is None else (g["w1"].to(to), g["w2"].to(to))
+        return lambda z: F.silu(z @ w1.t()) @ w2.t()
+    if g["sub"] == "silu_half":
+        return lambda z: F.silu(z) * 0.5
+    return lambda z: z
+
+
 def max_rel(ref: torch.Tensor, got: torch.Tensor) -> float:
     """max|ref - got| / max|ref| (the reference's own `_check` relative measure,
     model/mhc_fused.py:871-876)."""

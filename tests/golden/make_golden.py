@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the oracle and the CUDA path.
 
 Runs the REFERENCE implementation itself (Tshirt-hfk/minimind-mhc, imported
-from a read-only checkout given by ``--reference``, default ``/root/reference``)
+from a read-only checkout given by ``--reference``)
 on small seeded CPU inputs and stores inputs, outputs and autograd gradients
 under ``tests/golden/*.pt``.  The reference has no golden vectors or
 known-answer tests of its own; its self-tests compare its Triton kernels with
@@ -40,7 +40,7 @@ def _rand_like_list(ts, gen):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of a read-only checkout of the reference")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from model import mhc_fused as R            # noqa: E402  (reference)
@@ -256,6 +256,42 @@ def main():
         n=n, C=c, iters=20, x_sum=x1.double().sum(), x_sq=x1.double().pow(2).sum(),
         phi_sum=phi1.double().sum(), rows=rows, out_rows=y1.view(1024, -1)[rows].clone(),
         out_sum=y1.double().sum(), out_sq=y1.double().pow(2).sum())
+
+    # ---------------- widths that take the sm_100a kernels ------------------------
+    # n*C a multiple of 512 and C a multiple of 128: the fused tcgen05 forward and
+    # the tensor-core backward run on these (the small cases above take the
+    # generic kernels).  bf16 throughout, as the reference runs only with matching
+    # activation / parameter dtypes; 136 tokens = one full and one partial
+    # 128-token tile; an elementwise sublayer keeps the fixture small.
+    gw = torch.Generator().manual_seed(4321)
+
+    def module_wide_case(kind, n, c, iters, t=136):
+        torch.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gw)))
+        if kind == "full":
+            mod = R.MHCConnection_Fused(n, c, sinkhorn_iters=iters)
+            with torch.no_grad():
+                mod.phi_weight.copy_(torch.randn(n * c, 2 * n + n * n, generator=gw) * 0.02)
+                mod.bias_res.add_(torch.randn(n, n, generator=gw) * 0.1)
+        else:
+            mod = RN.MHCConnection_FusedNoHres(n, c)
+            with torch.no_grad():
+                mod.phi_weight.copy_(torch.randn(n * c, 2 * n, generator=gw) * 0.02)
+        with torch.no_grad():
+            mod.bias_pre.copy_(torch.randn(n, generator=gw) * 0.1)
+            mod.bias_post.copy_(torch.randn(n, generator=gw) * 0.1)
+        mod = mod.to(torch.bfloat16)
+        x = torch.randn(1, t, n * c, generator=gw).bfloat16().requires_grad_(True)
+        y = mod._forward_ref(x, lambda z: F.silu(z) * 0.5)
+        loss = y.float().pow(2).mean()
+        names = [k for k, _ in mod.named_parameters()]
+        leaves = [x] + [p for _, p in mod.named_parameters()]
+        g = torch.autograd.grad(loss, leaves)
+        return dict(n=n, C=c, iters=iters, sub="silu_half", x=x.detach(), w1=None, w2=None,
+                    param_names=names, params=[p.detach().clone() for _, p in mod.named_parameters()],
+                    out=y.detach(), loss=loss.detach(), grads=[t.detach() for t in g])
+
+    out["module_full_bf16_c768_wide"] = module_wide_case("full", 4, 768, 20)
+    out["module_nohres_bf16_c1024_wide"] = module_wide_case("nohres", 4, 1024, 0)
 
     path = os.path.join(HERE, "golden.pt")
     torch.save(out, path)

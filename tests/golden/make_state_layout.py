@@ -3,8 +3,8 @@ and a few (n, C), the state_dict keys with shape and dtype, and the values of
 the parameters whose initialisation is deterministic (gate scales and
 biases).  A checkpoint written by the reference trainer (a state_dict, saved in
 fp16 by trainer/train_pretrain.py:63-71) loads into this build's modules only
-if these match.  Imports the reference from ``--reference`` (default
-/root/reference, read-only) and writes tests/golden/state_layout.json::
+if these match.  Imports the reference from ``--reference`` (a read-only
+checkout) and writes tests/golden/state_layout.json::
 
     python tests/golden/make_state_layout.py --reference /path/to/minimind-mhc
 """
@@ -21,7 +21,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of a read-only checkout of the reference")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch

@@ -1,4 +1,4 @@
-"""Checkpoint compatibility with the reference.
+"""Checkpoint compatibility with the reference (trainer checkpoint format).
 
 The reference trainer saves plain state_dicts, in fp16
 (trainer/train_pretrain.py:63-71) and reloads them with load_state_dict

@@ -11,7 +11,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from conftest import assert_close
+from conftest import assert_close, golden_sublayer
 
 pytestmark = pytest.mark.gpu
 
@@ -78,12 +78,17 @@ def _module_case(g, mod, k):
         for p, v in zip(mod.parameters(), g["params"]):
             p.copy_(v.to(p.dtype))
     x = g["x"].to(DEV).requires_grad_(True)
-    fn = _mlp(g["w1"].to(DEV), g["w2"].to(DEV)) if g["sub"] == "mlp" else (lambda z: z)
+    fn = golden_sublayer(g, DEV)
+    from model import _native as nat
     y = mod(x, fn)
+    if k.endswith("_wide"):
+        assert nat.lib().mhc_last_path() == 1, "the fused sm_100a forward did not run"
     assert_close(k + ".out", g["out"], y, atol, rtol)
     loss = y.float().pow(2).mean()
     ps = [p for _, p in mod.named_parameters()]
     gr = torch.autograd.grad(loss, [x] + ps)
+    if k.endswith("_wide"):
+        assert nat.lib().mhc_last_path() == 1, "the tensor-core backward did not run"
     names = ["x"] + [n for n, _ in mod.named_parameters()]
     for name, a, b in zip(names, g["grads"], gr):
         mult = 1 if name == "x" else 5

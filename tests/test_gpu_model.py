@@ -1,7 +1,17 @@
-"""The model-level benchmark workloads (bench.py --workload c4 / c5) on a
-small decoder: forward and one training step run through this build's mHC
-modules, the loss is finite and every mHC parameter receives a finite,
-non-zero gradient."""
+"""The model-level workloads (bench.py --workload c4 / c5) and the drop-in
+inside the reference's block structure.
+
+* The benchmark decoder has the reference ``MiniMindForCausalLM``'s state_dict
+  layout, so the reference's own weights (tests/golden/model_golden.pt, made
+  by tests/golden/make_model_golden.py from the reference run on the CPU in
+  fp32) load with ``strict=True``; its logits, next-token loss (plus the MoE
+  auxiliary loss) and mHC parameter gradients must match the reference's.
+  fp32 runs take the generic kernels and must agree to 1e-4 relative; the bf16
+  run (mHC parameters fp32, as in the benchmark) takes the sm_100a kernels
+  (n*C = 512) and must agree within the bf16 tolerance.
+* A small bf16 decoder trains through the kernels with finite, non-zero mHC
+  gradients.
+"""
 
 import os
 import sys
@@ -10,10 +20,71 @@ import pytest
 import torch
 import torch.nn.functional as F
 
+from conftest import ROOT, max_rel
+
 pytestmark = pytest.mark.gpu
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden", "model_golden.pt")
+
+
+def _golden():
+    return torch.load(GOLDEN, weights_only=False)
+
+
+def _decoder_for(kw, dtype):
+    import bench
+    return bench._build_decoder(
+        moe=bool(kw.get("use_moe", False)), dev=torch.device("cuda"), n=kw["mhc_residual_expansion"],
+        hidden=kw["hidden_size"], layers=kw["num_hidden_layers"], heads=kw["num_attention_heads"],
+        kv_heads=kw["num_key_value_heads"], inter=kw["intermediate_size"], vocab=kw["vocab_size"],
+        experts=kw.get("num_experts", 4), topk=kw.get("num_experts_per_tok", 1),
+        moe_inter=kw.get("moe_intermediate_size"), theta=kw["rope_theta"], eps=kw["rms_norm_eps"],
+        iters=10, use_mhc=kw["use_mhc"], dtype=dtype)
+
+
+def _run(g, dtype):
+    from model import _native as nat
+    m = _decoder_for(g["config"], dtype)
+    sd = {k: v.float() for k, v in g["state_dict"].items()}
+    m.load_state_dict(sd, strict=True)
+    m.train()
+    ids = g["ids"].cuda()
+    logits = m(ids)
+    fwd_path = nat.lib().mhc_last_path()
+    loss = F.cross_entropy(logits[:, :-1].float().reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
+    aux = m.aux_loss()
+    total = loss + aux if aux is not None else loss
+    params = dict(m.named_parameters())
+    grads = torch.autograd.grad(total, [params[n] for n in g["grad_names"]])
+    bwd_path = nat.lib().mhc_last_path()
+    assert nat.device_error_code() == 0
+    return logits, loss, aux, grads, (fwd_path, bwd_path)
+
+
+@pytest.mark.parametrize("case", ["dense_mhc1", "moe_mhc2"])
+def test_decoder_loads_reference_weights_and_matches_fp32(case):
+    g = _golden()[case]
+    logits, loss, aux, grads, _ = _run(g, torch.float32)
+    assert max_rel(g["logits"], logits) < 1e-4
+    assert abs(float(loss) - float(g["loss"])) < 1e-4 * float(g["loss"])
+    if aux is not None:
+        assert abs(float(aux) - float(g["aux_loss"])) < 1e-4 * max(float(g["aux_loss"]), 1e-6)
+    for name, a, b in zip(g["grad_names"], g["grads"], grads):
+        err = (a.float() - b.float().cpu()).abs().max().item()
+        assert err < 1e-5 + 2e-3 * a.abs().max().item(), (name, err)
+
+
+@pytest.mark.parametrize("case", ["dense_mhc1", "moe_mhc2"])
+def test_decoder_bf16_on_fused_kernels_matches_reference(case):
+    g = _golden()[case]
+    logits, loss, _, grads, paths = _run(g, torch.bfloat16)
+    assert paths == (1, 1), "the sm_100a forward / tensor-core backward did not run"
+    assert max_rel(g["logits"], logits) < 5e-2
+    assert abs(float(loss) - float(g["loss"])) < 1e-2 * float(g["loss"])
+    for name, a, b in zip(g["grad_names"], g["grads"], grads):
+        assert max_rel(a, b) < 0.25, name
 
 
 @pytest.mark.parametrize("moe", [False, True], ids=["dense", "moe"])
@@ -27,10 +98,12 @@ def test_small_decoder_trains_through_mhc_kernels(moe):
     logits = m(ids)
     assert logits.shape == (2, 256, 512)
     loss = F.cross_entropy(logits.view(-1, 512).float(), ids.view(-1))
+    if moe:
+        loss = loss + m.aux_loss()
     assert torch.isfinite(loss)
     loss.backward()
     assert nat.lib().mhc_device_error(1) == 0
-    mhc = [(n, p) for n, p in m.named_parameters() if "mhc" in n or n.startswith("exit.0")]
+    mhc = [(n, p) for n, p in m.named_parameters() if "mhc" in n or n.startswith("model.norm.0")]
     assert mhc
     for n, p in mhc:
         assert p.dtype == torch.float32, n

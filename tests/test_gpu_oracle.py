@@ -252,3 +252,76 @@ def test_sinkhorn_backward_checkpoint_segments(n, iters):
     assert (y.double().cpu() - y64).abs().max().item() < 2e-6
     err = (dm.double().cpu() - dm64).abs().max().item()
     assert err < 1e-5 + 1e-4 * dm64.abs().max().item(), err
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "fp32"])
+def test_256k_tokens_sampled(dtype):
+    """The top of the config-2 token sweep, T = 262,144 (x is 1.6 GB in bf16 and
+    3.2 GB in fp32, so fp32 byte offsets pass 2^31).  bf16 takes the fused
+    kernel, fp32 the generic kernels.  Sampled tokens, the last ones included,
+    against the oracle; the doubly-stochastic property on every token."""
+    gen = torch.Generator().manual_seed(5)
+    n, c, t = 4, 768, 262144
+    torch.manual_seed(1)
+    xd = torch.randn(t, n * c, device=DEV, dtype=dtype)
+    p = _bench_params(n, c, True, gen)
+    z, h_pre, h_post, h_res, inv, mixes = _native_pre(xd, p, True, 20, n, c)
+    hr = h_res.double()
+    assert (hr.sum(-1) - 1).abs().max().item() < SK_TOL
+    assert (hr.sum(-2) - 1).abs().max().item() < SK_TOL
+    idx = torch.cat([torch.randperm(t, generator=gen)[:384], torch.arange(t - 16, t)])
+    sel = idx.to(DEV)
+    ref = _oracle_coefs(xd[sel].cpu(), p, True, 20, n, c)
+    assert max_rel(ref["inv_rms"], inv[sel]) < COEF_RTOL
+    assert max_rel(ref["h_pre"], h_pre[sel]) < COEF_RTOL
+    assert max_rel(ref["h_post"], h_post[sel]) < COEF_RTOL
+    assert max_rel(ref["h_res"], h_res[sel]) < COEF_RTOL
+    assert max_rel(ref["mixes"], mixes[sel]) < COEF_RTOL
+    assert max_rel(ref["z"], z[sel]) < (STREAM_RTOL if dtype == torch.bfloat16 else COEF_RTOL)
+
+
+def test_autocast_fp32_stream_module_fwd_bwd():
+    """The reference trainers' setting: fp32 weights under bf16 autocast
+    (trainer/train_pretrain.py:129-130).  The residual stream stays fp32
+    (embedding -> RMSNorm -> StreamExpand, model/model_minimind.py:365,
+    384-385) and the sublayer's output is bf16, so the layer sees x fp32 and f
+    bf16.  Forward and backward against fp32 oracle autograd, with the
+    sublayer's bf16 rounding reproduced on the CPU."""
+    from model.mhc_fused import MHCConnection_Fused
+    torch.manual_seed(6)
+    gen = torch.Generator().manual_seed(6)
+    n, c, t = 4, 768, 384
+    mod = MHCConnection_Fused(n, c, sinkhorn_iters=20)
+    with torch.no_grad():
+        for p in mod.parameters():
+            p.add_(torch.randn(p.shape, generator=gen) * 0.05)
+    w = torch.randn(c, c, generator=gen) / c ** 0.5
+    x = torch.randn(1, t, n * c, generator=gen)
+    gout = torch.randn(1, t, n * c, generator=gen)
+
+    ps = [p.detach().clone().requires_grad_(True) for p in mod.parameters()]
+    xo = x.clone().requires_grad_(True)
+    fo = lambda z: F.linear(z.bfloat16(), w.bfloat16()).float()  # noqa: E731  (autocast's casts)
+    yo = O.full_forward(xo, O.FullParams(*ps), fo, n, c, 20)
+    go = torch.autograd.grad(yo, [xo] + ps, gout)
+
+    modd = mod.to(DEV)
+    lin = torch.nn.Linear(c, c, bias=False).to(DEV)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    xd = x.to(DEV).requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        seen = {}
+
+        def fd(z):
+            seen["z"] = z.dtype
+            f = lin(z)
+            seen["f"] = f.dtype
+            return f
+        yd = modd(xd, fd)
+    assert seen == {"z": torch.float32, "f": torch.bfloat16} and yd.dtype == torch.float32
+    gd = torch.autograd.grad(yd, [xd] + list(modd.parameters()), gout.to(DEV))
+    assert_close("out", yo, yd, 1e-2, 1e-2)
+    names = ["x"] + [nm for nm, _ in mod.named_parameters()]
+    for nm, a, b in zip(names, go, gd):
+        assert_close("grad_" + nm, a, b, 5e-2, 5e-2)

@@ -8,7 +8,7 @@ reproduce it (same rounding points, same gradients through autograd).
 import torch
 import torch.nn.functional as F
 
-from conftest import assert_close
+from conftest import assert_close, golden_sublayer
 from oracle import mhc_oracle as O
 
 
@@ -68,7 +68,7 @@ def _module_check(g, forward, params_cls, k):
     x = g["x"].clone().requires_grad_(True)
     ps = [p.clone().requires_grad_(True) for p in g["params"]]
     assert tuple(g["param_names"]) == params_cls.NAMES
-    fn = _mlp(g["w1"], g["w2"]) if g["sub"] == "mlp" else (lambda z: z)
+    fn = golden_sublayer(g)
     y = forward(x, params_cls(*ps), fn)
     assert_close(k + ".out", g["out"], y, tol, tol)
     loss = y.float().pow(2).mean()
