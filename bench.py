@@ -13,6 +13,20 @@ Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a
 device synchronise, CUDA events on the launching stream, max over ranks.  x is
 201 MB per GPU (larger than the 126 MB L2), so every step streams from HBM.
 
+The same JSON line also carries, measured in the same run:
+  * "backward": the layer backward (merge backward + coefficient backward);
+  * "pre_two_read": the previous fused forward kernel on the same inputs;
+  * "e2e": the layer through the C-ABI from pinned host buffers, with the
+    host link's copy-only ceiling;
+  * "sweep": configs[1]'s token sweep, 4K to 256K tokens per GPU (L2 flushed
+    between steps where the inputs would fit in it);
+  * "nohres_c768", "nohres_c1024": configs[2], the no-H_res layer, forward and
+    backward;
+  * "fp32_stream": the layer with an fp32 residual stream and a bf16 sublayer
+    output, the setting of the reference's bf16-autocast trainers;
+  * "train_step": configs[4], the MoE + mHC training step (8 x 2048 tokens per
+    GPU), with the NCCL gradient all-reduce timed on its own.
+
 Multi-GPU: one process per GPU (torchrun), tokens sharded (weak scaling): every
 rank runs its own 16 x 2048 tokens with no collective on the data path.
 
@@ -52,79 +66,48 @@ def _peaks():
         return 6650.0, "fallback"
 
 
-def _time_backward(L, nat, x, ps, with_res, iters, z, h_post, h_res, inv_rms, mixes, f_out, t, n, c, fd, dev,
-                   sptr, stream, steps, peak_of):
-    """Backward of one layer through the C-ABI: mhc_post_bwd (merge) then
-    mhc_pre_bwd (coefficients, Sinkhorn by recompute, RMSNorm, dphi / dalpha /
-    dbias reductions).  dz stands in for the sublayer's input gradient.
-    Algorithmic bytes per token s*(6nC + 3C)."""
-    gen = torch.Generator(device=dev).manual_seed(99)
-    dout = torch.randn(t, n * c, device=dev, dtype=torch.bfloat16, generator=gen)
-    dz = torch.randn(t, c, device=dev, dtype=torch.bfloat16, generator=gen)
-    dx_post = torch.empty_like(x)
-    dx = torch.empty_like(x)
-    dh_res = torch.empty(t, n * n, device=dev) if with_res else None
-    dh_post = torch.empty(t, n, device=dev)
-    df = torch.empty_like(f_out)
-    gps = [torch.empty_like(p, dtype=torch.float32) for p in ps]
-    g_res = (gps[5], gps[6]) if with_res else (None, None)
-    a_res, b_res = (ps[5], ps[6]) if with_res else (None, None)
-    ws = nat.workspace(L.mhc_pre_bwd_workspace(t, n, c, int(with_res), int(with_res), iters), dev)
-
-    def step():
-        st = L.mhc_post_bwd(nat.ptr(dout), nat.ptr(x), nat.BF16, nat.ptr(h_res), nat.F32, nat.ptr(h_post),
-                            nat.F32, nat.ptr(f_out), nat.BF16, nat.ptr(dx_post), nat.ptr(dh_res), nat.ptr(dh_post),
-                            nat.ptr(df), t, n, c, sptr)
-        nat.check(st, "mhc_post_bwd")
-        st = L.mhc_pre_bwd(nat.ptr(x), nat.BF16, t, n, c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]),
-                           nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32,
-                           int(with_res), int(with_res), iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(inv_rms),
-                           nat.ptr(mixes), nat.ptr(dz), None, nat.ptr(dh_post), nat.ptr(dh_res), nat.F32,
-                           nat.ptr(dx_post), nat.ptr(dx), nat.ptr(gps[0]), nat.ptr(gps[1]), nat.ptr(gps[2]),
-                           nat.ptr(gps[3]), nat.ptr(gps[4]), nat.ptr(g_res[0]), nat.ptr(g_res[1]), nat.ptr(ws),
-                           ws.numel(), sptr)
-        nat.check(st, "mhc_pre_bwd")
-
-    for _ in range(3):
-        step()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    torch.cuda.synchronize(dev)
-    for e0, e1 in ev:
-        e0.record(stream)
-        step()
-        e1.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = sorted(e0.elapsed_time(e1) for e0, e1 in ev)[len(ev) // 2]
-    bytes_tok = 2 * (6 * n * c + 3 * c)
-    peak, kind = peak_of()
-    gbs = bytes_tok * t / (ms / 1e3) / 1e9
-    return {"ms_per_step": ms, "tokens_per_s": t / (ms / 1e3), "algorithmic_bytes_per_token": bytes_tok,
-            "gbs": gbs, "frac_of_measured": gbs / peak, "steps": steps,
-            "calls": "mhc_post_bwd + mhc_pre_bwd (median step, CUDA events)"}
-
-
-def _profiled_traffic(kernel, n, c, t, with_res):
-    """DRAM bytes (read + write) per launch of the dominant kernel, from the
-    committed ncu summary of this exact workload (profiles/*.md carries a line
-    `traffic_bytes_per_launch: <int>`); None for other workloads."""
-    if (n, c, t, bool(with_res)) != (4, 768, 32768, True):
-        return None
-    name = {"pre": "pre_tc_kernel_config2.md", "post": "post_fwd_kernel_config2.md"}[kernel]
-    path = os.path.join(ROOT, "profiles", name)
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return int(line.split(":", 1)[1]), "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/" + name
-    except OSError:
-        pass
-    return None
-
-
 def _layer_bytes(n, c, s, with_res):
     """Algorithmic bytes per token of the forward layer: read x twice (pre and
     post), write z, read f, write x' -> s * (3nC + 2C)."""
     return s * (3 * n * c + 2 * c)
+
+
+def _fwd_bytes(n, c, sx, sf):
+    """Forward bytes per token with x (and z, x') of sx bytes and f of sf bytes:
+    pre reads x and writes z, post reads x and f and writes x'."""
+    return sx * (3 * n * c + c) + sf * c
+
+
+def _bwd_bytes(n, c, sx, sf):
+    """Backward bytes per token: the merge backward reads dx', x, f and writes
+    dx_post, df; the coefficient backward reads x, dz, dx_post and writes dx."""
+    return sx * (6 * n * c + c) + sf * 2 * c
+
+
+def _profiled_traffic(kernel, n, c, t, with_res):
+    """DRAM bytes (read + write) per launch of the dominant kernel from the
+    committed ncu summary of this exact workload (profiles/*.md carries a line
+    `traffic_bytes_per_launch: <int>` and the commit the capture was made at);
+    None for other workloads.  This is a profiled figure, not measured in this
+    run."""
+    if (n, c, t, bool(with_res)) != (4, 768, 32768, True):
+        return None
+    name = {"pre": "pre_sr_kernel_config2.md", "post": "post_fwd_kernel_config2.md"}[kernel]
+    path = os.path.join(ROOT, "profiles", name)
+    out = {}
+    try:
+        with open(path) as f:
+            for line in f:
+                for key in ("traffic_bytes_per_launch", "captured_at_commit"):
+                    if line.startswith(key + ":"):
+                        out[key] = line.split(":", 1)[1].strip()
+    except OSError:
+        return None
+    if "traffic_bytes_per_launch" not in out:
+        return None
+    return (int(out["traffic_bytes_per_launch"]),
+            f"profiled: ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{name}, "
+            f"captured at commit {out.get('captured_at_commit', 'unknown')}")
 
 
 class ClockSampler:
@@ -194,13 +177,25 @@ class ClockSampler:
                 "samples": len(self.samples), "reasons": sorted(reasons)}
 
 
-def _cpu_reference(n, c, tokens, budget_s, min_runs, max_runs):
-    """The reference's pure-PyTorch path (oracle restatement), fp32, f = identity."""
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def _cpu_reference(n, c, tokens, budget_s, min_runs, max_runs, dtype=torch.float32):
+    """The reference's pure-PyTorch path (oracle restatement), f = identity,
+    on a bounded token sample; returns the per-run wall times."""
     from oracle import mhc_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(0)
-    x = torch.randn(1, tokens, n * c, generator=gen)
-    p = O.make_full_params(n, c, generator=gen)
+    x = torch.randn(1, tokens, n * c, generator=gen).to(dtype)
+    p = O.make_full_params(n, c, generator=gen, dtype=dtype)
     with torch.no_grad():
         O.full_forward(x, p, lambda z: z, n, c, 20)  # warm-up
         times = []
@@ -247,68 +242,185 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+class LayerBench:
+    """One mHC layer's buffers and its C-ABI calls: the forward (mhc_pre_fwd,
+    then mhc_post_fwd) and the backward (mhc_post_bwd, then mhc_pre_bwd),
+    launched on `stream`.  x ~ N(0, 1) in `x_dtype`, phi ~ N(0, 0.02), all
+    alpha = 0.01, biases 0, 20 Sinkhorn iterations when the layer has H_res;
+    the sublayer output f is a random-init SwiGLU C -> 2048 -> C of z in torch
+    (bf16 weights, output in `f_dtype`), evaluated once before timing."""
+
+    def __init__(self, t, n, c, with_res, x_dtype, f_dtype, dev, stream, seed):
+        import torch.nn.functional as F
+
+        from model import _native as nat
+        from model.mhc_fused import _params
+        self.nat, self.L = nat, nat.lib()
+        self.t, self.n, self.c, self.with_res = t, n, c, with_res
+        self.iters = 20 if with_res else 0
+        self.fd = 2 * n + (n * n if with_res else 0)
+        self.sptr = stream.cuda_stream
+        self.xc, self.fc = nat.dtype_code(x_dtype), nat.dtype_code(f_dtype)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.x = torch.randn(t, n * c, device=dev, generator=g).to(x_dtype)
+        a = torch.tensor(0.01, device=dev)
+        bn = torch.zeros(n, device=dev)
+        ps = [torch.randn(n * c, self.fd, device=dev, generator=g) * 0.02, a, bn, a.clone(), bn.clone()]
+        if with_res:
+            ps += [a.clone(), torch.zeros(n, n, device=dev)]
+        self.ps = _params(*ps)
+        self.z = torch.empty(t, c, device=dev, dtype=x_dtype)
+        self.h_post = torch.empty(t, n, device=dev)
+        self.h_res = torch.empty(t, n, n, device=dev) if with_res else None
+        self.inv = torch.empty(t, device=dev)
+        self.mix = torch.empty(t, self.fd, device=dev)
+        self.out = torch.empty_like(self.x)
+        self.ws = nat.workspace(self.L.mhc_pre_fwd_workspace(t, n, c, int(with_res)), dev)
+        self.pre()
+        w1 = torch.randn(2048, c, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
+        w2 = torch.randn(2048, c, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
+        w3 = torch.randn(c, 2048, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
+        zb = self.z.to(torch.bfloat16)
+        self.f = ((F.silu(zb @ w1.t()) * (zb @ w2.t())) @ w3.t()).to(f_dtype)
+        self.pre_path = self.L.mhc_last_path()
+        self._bwd_ready = False
+
+    def pre(self, x=None):
+        nat, ps = self.nat, self.ps
+        a_res, b_res = (ps[5], ps[6]) if self.with_res else (None, None)
+        st = self.L.mhc_pre_fwd(nat.ptr(self.x if x is None else x), self.xc, self.t, self.n, self.c,
+                                nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]), nat.ptr(ps[3]), nat.ptr(ps[4]),
+                                nat.ptr(a_res), nat.ptr(b_res), nat.F32, int(self.with_res), int(self.with_res),
+                                self.iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(self.z), None, nat.ptr(self.h_post),
+                                nat.ptr(self.h_res), nat.F32, nat.ptr(self.inv), nat.ptr(self.mix),
+                                nat.ptr(self.ws), self.ws.numel(), self.sptr)
+        nat.check(st, "mhc_pre_fwd")
+
+    def post(self):
+        nat = self.nat
+        st = self.L.mhc_post_fwd(nat.ptr(self.x), self.xc, nat.ptr(self.h_res), nat.F32, nat.ptr(self.h_post),
+                                 nat.F32, nat.ptr(self.f), self.fc, nat.ptr(self.out), self.t, self.n, self.c,
+                                 0, 0, 0.0, None, self.sptr)
+        nat.check(st, "mhc_post_fwd")
+
+    def _bwd_buffers(self):
+        dev = self.x.device
+        g = torch.Generator(device=dev).manual_seed(99)
+        self.dout = torch.randn(self.x.shape, device=dev, generator=g).to(self.x.dtype)
+        self.dz = torch.randn(self.z.shape, device=dev, generator=g).to(self.z.dtype)
+        self.dx_post = torch.empty_like(self.x)
+        self.dx = torch.empty_like(self.x)
+        self.dh_res = torch.empty(self.t, self.n * self.n, device=dev) if self.with_res else None
+        self.dh_post = torch.empty(self.t, self.n, device=dev)
+        self.df = torch.empty_like(self.f)
+        self.gps = [torch.empty_like(p, dtype=torch.float32) for p in self.ps]
+        self.bws = self.nat.workspace(self.L.mhc_pre_bwd_workspace(self.t, self.n, self.c, int(self.with_res),
+                                                                   int(self.with_res), self.iters), dev)
+        self._bwd_ready = True
+
+    def bwd(self):
+        if not self._bwd_ready:
+            self._bwd_buffers()
+        nat, ps, gps = self.nat, self.ps, self.gps
+        a_res, b_res = (ps[5], ps[6]) if self.with_res else (None, None)
+        g_res = (gps[5], gps[6]) if self.with_res else (None, None)
+        st = self.L.mhc_post_bwd(nat.ptr(self.dout), nat.ptr(self.x), self.xc, nat.ptr(self.h_res), nat.F32,
+                                 nat.ptr(self.h_post), nat.F32, nat.ptr(self.f), self.fc, nat.ptr(self.dx_post),
+                                 nat.ptr(self.dh_res), nat.ptr(self.dh_post), nat.ptr(self.df), self.t, self.n,
+                                 self.c, self.sptr)
+        nat.check(st, "mhc_post_bwd")
+        st = self.L.mhc_pre_bwd(nat.ptr(self.x), self.xc, self.t, self.n, self.c, nat.ptr(ps[0]), nat.ptr(ps[1]),
+                                nat.ptr(ps[2]), nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res),
+                                nat.F32, int(self.with_res), int(self.with_res), self.iters, 2.0, 1e-6, 1e-6, 1e-6,
+                                nat.ptr(self.inv), nat.ptr(self.mix), nat.ptr(self.dz), None, nat.ptr(self.dh_post),
+                                nat.ptr(self.dh_res), nat.F32, nat.ptr(self.dx_post), nat.ptr(self.dx),
+                                nat.ptr(gps[0]), nat.ptr(gps[1]), nat.ptr(gps[2]), nat.ptr(gps[3]),
+                                nat.ptr(gps[4]), nat.ptr(g_res[0]), nat.ptr(g_res[1]), nat.ptr(self.bws),
+                                self.bws.numel(), self.sptr)
+        nat.check(st, "mhc_pre_bwd")
+
+    def input_bytes(self):
+        return self.x.numel() * self.x.element_size()
+
+
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
+
+
+def _time_steps(fns, steps, warmup, stream, flush=None):
+    """Per-step device time of calling `fns` in order, CUDA events on `stream`
+    around each step (and around each fn).  With `flush`, a buffer larger than
+    L2 is rewritten between steps, outside the events.  Returns (median step
+    ms, mean ms per fn)."""
+    for _ in range(warmup):
+        for fn in fns:
+            fn()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)] for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        if flush is not None:
+            flush.add_(1)
+        ev[i][0].record(stream)
+        for k, fn in enumerate(fns):
+            fn()
+            ev[i][k + 1].record(stream)
+    torch.cuda.synchronize()
+    step = sorted(e[0].elapsed_time(e[-1]) for e in ev)[steps // 2]
+    per = [sum(e[k].elapsed_time(e[k + 1]) for e in ev) / steps for k in range(len(fns))]
+    return step, per
+
+
+def _max_over_ranks(v, world, dev):
+    if world <= 1:
+        return v
+    import torch.distributed as dist
+    tt = torch.tensor([float(v)], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return float(tt.item())
+
+
+def _layer_entry(lb, world, dev, steps, warmup, stream, peak, flush, with_bwd, sx, sf):
+    """Forward (and backward) throughput of one LayerBench, whole job."""
+    fl = flush if lb.input_bytes() < L2_FLUSH_BYTES else None
+    f_ms, (pre_ms, post_ms) = _time_steps([lb.pre, lb.post], steps, warmup, stream, fl)
+    f_ms = _max_over_ranks(f_ms, world, dev)
+    n, c, t = lb.n, lb.c, lb.t
+    fb = _fwd_bytes(n, c, sx, sf)
+    e = {"tokens_per_gpu": t, "tokens_per_s": world * t / (f_ms / 1e3), "ms_per_step": f_ms,
+         "algorithmic_bytes_per_token": fb, "hbm_gbs_per_gpu": fb * t / (f_ms / 1e3) / 1e9,
+         "frac_of_measured": fb * t / (f_ms / 1e3) / 1e9 / peak,
+         "per_call_ms": {"pre": pre_ms, "post": post_ms}, "pre_path": lb.pre_path,
+         "l2": "flushed between steps" if fl is not None else "inputs larger than L2"}
+    if with_bwd:
+        b_ms, _ = _time_steps([lb.bwd], max(5, steps // 2), 3, stream, fl)
+        b_ms = _max_over_ranks(b_ms, world, dev)
+        bb = _bwd_bytes(n, c, sx, sf)
+        e["backward"] = {"ms_per_step": b_ms, "tokens_per_s": world * t / (b_ms / 1e3),
+                         "algorithmic_bytes_per_token": bb,
+                         "frac_of_measured": bb * t / (b_ms / 1e3) / 1e9 / peak,
+                         "bwd_path": lb.L.mhc_last_path()}
+    return e
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
-    import torch.nn.functional as F
 
     from model import _native as nat
-    from model.mhc_fused import _params
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = _peaks()
     n, c = 4, 768
     with_res = args.variant == "full"
     if args.variant == "nohres" and args.C:
         c = args.C
     t = args.tokens
-    iters = 20 if with_res else 0
-    fd = 2 * n + (n * n if with_res else 0)
     torch.manual_seed(1234 + rank)
-    x = torch.randn(t, n * c, device=dev, dtype=torch.bfloat16)
-    phi = torch.randn(n * c, fd, device=dev) * 0.02
-    a = torch.tensor(0.01, device=dev)
-    bn = torch.zeros(n, device=dev)
-    ps = [phi, a, bn, a.clone(), bn.clone()] + ([a.clone(), torch.zeros(n, n, device=dev)] if with_res else [])
-    ps = _params(*ps)
-    # sublayer f = SwiGLU 768 -> 2048 -> 768 (torch), evaluated once outside the timed region
-    w_gate = torch.randn(2048, c, device=dev, dtype=torch.bfloat16) * 0.02
-    w_up = torch.randn(2048, c, device=dev, dtype=torch.bfloat16) * 0.02
-    w_down = torch.randn(c, 2048, device=dev, dtype=torch.bfloat16) * 0.02
-
-    z = torch.empty(t, c, device=dev, dtype=torch.bfloat16)
-    h_post = torch.empty(t, n, device=dev)
-    h_res = torch.empty(t, n, n, device=dev) if with_res else None
-    inv_rms = torch.empty(t, device=dev)
-    mixes = torch.empty(t, fd, device=dev)
-    out = torch.empty_like(x)
-    ws = nat.workspace(nat.lib().mhc_pre_fwd_workspace(t, n, c, int(with_res)), dev)
-    stream = torch.cuda.current_stream(dev)
-    sptr = stream.cuda_stream
-    L = nat.lib()
-    a_res, b_res = (ps[5], ps[6]) if with_res else (None, None)
-
-    # the module's forward path: the coefficient kernel (with Sinkhorn-Knopp and
-    # the pre-aggregate fused in), then the res / post merge
-    def pre(xin):
-        st = L.mhc_pre_fwd(nat.ptr(xin), nat.BF16, t, n, c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]),
-                           nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32,
-                           int(with_res), int(with_res), iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(z), None,
-                           nat.ptr(h_post), nat.ptr(h_res), nat.F32, nat.ptr(inv_rms), nat.ptr(mixes),
-                           nat.ptr(ws), ws.numel(), sptr)
-        nat.check(st, "mhc_pre_fwd")
-
-    def post(xin, f, o):
-        st = L.mhc_post_fwd(nat.ptr(xin), nat.BF16, nat.ptr(h_res), nat.F32, nat.ptr(h_post), nat.F32,
-                            nat.ptr(f), nat.BF16, nat.ptr(o), t, n, c, 0, 0, 0.0, None, sptr)
-        nat.check(st, "mhc_post_fwd")
-
-    pre(x)
-    f_out = (F.silu(z @ w_gate.t()) * (z @ w_up.t())) @ w_down.t()
-    post(x, f_out, out)
-    torch.cuda.synchronize(dev)
-
-    fused = bool(L.mhc_last_path())
-    launches_per_step = 2 if fused else 3  # fused coefficient+aggregate (or 2 generic kernels), merge
+    lb = LayerBench(t, n, c, with_res, torch.bfloat16, torch.bfloat16, dev, stream, 1234 + rank)
+    L = lb.L
+    x, out = lb.x, lb.out
+    fused_path = lb.pre_path
+    launches_per_step = 2 if fused_path else 3  # fused coefficient+aggregate (or 2 generic kernels), merge
     bytes_tok = _layer_bytes(n, c, 2, with_res)
     pre_bytes = 2 * (n * c + c)
     post_bytes = 2 * (2 * n * c + c)
@@ -318,8 +430,8 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
 
     for _ in range(args.warmup):
-        pre(x)
-        post(x, f_out, out)
+        lb.pre()
+        lb.post()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     sampler = ClockSampler(dev)
@@ -334,119 +446,79 @@ def run_ours(args, rank, world, local_rank):
     for i in range(args.steps):
         e0, e1, e2 = ev[i]
         e0.record(stream)
-        pre(x)
+        lb.pre()
         e1.record(stream)
-        post(x, f_out, out)
+        lb.post()
         e2.record(stream)
     t_stop.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
-    total_ms = t_start.elapsed_time(t_stop)
+    total_ms = _max_over_ranks(t_start.elapsed_time(t_stop), world, dev)
     pre_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev]
     post_ms = [e1.elapsed_time(e2) for _, e1, e2 in ev]
-    if world > 1:
-        tt = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms = tt.item()
+
+    # ---- the two-read fused kernel on the same inputs, for comparison ---------
+    two_read = None
+    if fused_path == 2:
+        prev = L.mhc_set_path_policy(nat.PATH_TWO_READ)
+        tr_ms, (tr_pre,) = _time_steps([lb.pre], max(10, args.steps // 4), 3, stream)
+        two_read = {"pre_ms": tr_pre, "path": L.mhc_last_path(),
+                    "note": "x read from HBM by TMA, then again from L2 (the previous design)"}
+        L.mhc_set_path_policy(prev)
+        lb.pre()
 
     # ---- backward of the layer (training config), reported beside the forward --
     bwd = None
     if not args.no_bwd:
-        bwd = _time_backward(L, nat, x, ps, with_res, iters, z, h_post, h_res, inv_rms, mixes, f_out,
-                             t, n, c, fd, dev, sptr, stream, max(3, min(args.steps, 20)), peak_of=_peaks)
+        b_ms, _ = _time_steps([lb.bwd], max(3, min(args.steps, 20)), 3, stream)
+        b_ms = _max_over_ranks(b_ms, world, dev)
+        bb = _bwd_bytes(n, c, 2, 2)
+        gbs = bb * t / (b_ms / 1e3) / 1e9
+        bwd = {"ms_per_step": b_ms, "tokens_per_s": world * t / (b_ms / 1e3), "algorithmic_bytes_per_token": bb,
+               "gbs": gbs, "frac_of_measured": gbs / peak, "bwd_path": L.mhc_last_path(),
+               "calls": "mhc_post_bwd + mhc_pre_bwd (median step, CUDA events)"}
 
     # ---- end to end through the public API with host buffers -------------------
     # A step copies x and f from pinned host memory, runs mhc_pre_fwd and
     # mhc_post_fwd through the C-ABI and copies x' back.  The batch goes in
     # E2E_CHUNKS token chunks rotated over E2E_STREAMS streams, so one chunk's
     # host-to-device copy overlaps another's device-to-host copy (separate copy
-    # engines) and the kernels; every byte is still copied inside the step.
+    # engines) and the kernels; every byte is still copied inside the step.  The
+    # same copies without the kernels give the host link's ceiling.
     e2e = None
     if not args.no_e2e:
-        E2E_CHUNKS, E2E_STREAMS = 8, 3
-        x_h = x.cpu().pin_memory()
-        f_h = f_out.cpu().pin_memory()
-        o_h = torch.empty_like(x_h).pin_memory()
-        bounds = [t * i // E2E_CHUNKS for i in range(E2E_CHUNKS + 1)]
-        cmax = max(bounds[i + 1] - bounds[i] for i in range(E2E_CHUNKS))
-        streams = [torch.cuda.Stream(dev) for _ in range(E2E_STREAMS)]
-        slots = []
-        for _ in range(E2E_STREAMS):
-            slots.append(dict(
-                x=torch.empty(cmax, n * c, device=dev, dtype=torch.bfloat16),
-                f=torch.empty(cmax, c, device=dev, dtype=torch.bfloat16),
-                o=torch.empty(cmax, n * c, device=dev, dtype=torch.bfloat16),
-                z=torch.empty(cmax, c, device=dev, dtype=torch.bfloat16),
-                hp=torch.empty(cmax, n, device=dev), hr=torch.empty(cmax, n, n, device=dev) if with_res else None,
-                inv=torch.empty(cmax, device=dev), mix=torch.empty(cmax, fd, device=dev),
-                ws=nat.workspace(L.mhc_pre_fwd_workspace(cmax, n, c, int(with_res)), dev)))
+        e2e = _e2e(lb, args, world, dev, stream, barrier)
 
-        def chunk(k):
-            lo, hi = bounds[k], bounds[k + 1]
-            m = hi - lo
-            st = streams[k % E2E_STREAMS]
-            sl = slots[k % E2E_STREAMS]
-            sp = st.cuda_stream
-            with torch.cuda.stream(st):
-                sl["x"][:m].copy_(x_h[lo:hi], non_blocking=True)
-                sl["f"][:m].copy_(f_h[lo:hi], non_blocking=True)
-            r = L.mhc_pre_fwd(nat.ptr(sl["x"]), nat.BF16, m, n, c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]),
-                              nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32,
-                              int(with_res), int(with_res), iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(sl["z"]), None,
-                              nat.ptr(sl["hp"]), nat.ptr(sl["hr"]), nat.F32, nat.ptr(sl["inv"]), nat.ptr(sl["mix"]),
-                              nat.ptr(sl["ws"]), sl["ws"].numel(), sp)
-            nat.check(r, "mhc_pre_fwd")
-            r = L.mhc_post_fwd(nat.ptr(sl["x"]), nat.BF16, nat.ptr(sl["hr"]), nat.F32, nat.ptr(sl["hp"]), nat.F32,
-                               nat.ptr(sl["f"]), nat.BF16, nat.ptr(sl["o"]), m, n, c, 0, 0, 0.0, None, sp)
-            nat.check(r, "mhc_post_fwd")
-            with torch.cuda.stream(st):
-                o_h[lo:hi].copy_(sl["o"][:m], non_blocking=True)
-
-        def e2e_step():
-            go = torch.cuda.Event()
-            go.record(stream)
-            for st in streams:
-                st.wait_event(go)
-            for k in range(E2E_CHUNKS):
-                chunk(k)
-            for st in streams:
-                done = torch.cuda.Event()
-                done.record(st)
-                stream.wait_event(done)
-
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
-        barrier()
-        torch.cuda.synchronize(dev)
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        k_e2e = max(1, min(args.steps, 5))
-        for _ in range(k_e2e):
-            e2e_step()
-        s1.record(stream)
-        torch.cuda.synchronize(dev)
-        barrier()
-        e_ms = s0.elapsed_time(s1)
-        if world > 1:
-            tt = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            e_ms = tt.item()
-        # spot-check the copied-back result against the device-side step's
-        pre(x)
-        post(x, f_out, out)
-        torch.cuda.synchronize(dev)
-        e2e_ok = bool(torch.equal(o_h.to(dev), out))  # every chunk, every stream slot
-        e2e = {"value": world * t * k_e2e / (e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(x_h.numel() * 2 + f_h.numel() * 2),
-               "d2h_bytes_per_step": int(o_h.numel() * 2), "steps": k_e2e,
-               "ms_per_step": e_ms / k_e2e,
-               "pipeline": f"{E2E_CHUNKS} token chunks over {E2E_STREAMS} streams (H2D / kernels / D2H overlap)",
-               "result_matches_device_step": e2e_ok}
+    # ---- sub-measurements of the other BASELINE configurations ----------------
+    extra = {}
+    if not args.no_extra and args.variant == "full" and t == 16 * 2048:
+        flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+        del lb
+        torch.cuda.empty_cache()
+        sweep = {}
+        for ts in (4096, 16384, 65536, 262144):
+            lbs = LayerBench(ts, n, c, True, torch.bfloat16, torch.bfloat16, dev, stream, 77 + rank)
+            sweep[str(ts)] = _layer_entry(lbs, world, dev, 20, 3, stream, peak, flush, False, 2, 2)
+            del lbs
+            torch.cuda.empty_cache()
+        extra["sweep"] = sweep
+        for cc in (768, 1024):
+            lbs = LayerBench(t, n, cc, False, torch.bfloat16, torch.bfloat16, dev, stream, 88 + rank)
+            extra[f"nohres_c{cc}"] = _layer_entry(lbs, world, dev, 20, 3, stream, peak, flush, True, 2, 2)
+            del lbs
+            torch.cuda.empty_cache()
+        lbs = LayerBench(t, n, c, True, torch.float32, torch.bfloat16, dev, stream, 99 + rank)
+        extra["fp32_stream"] = _layer_entry(lbs, world, dev, 20, 3, stream, peak, flush, True, 4, 2)
+        extra["fp32_stream"]["setting"] = ("x fp32, f bf16: the residual stream under the reference trainers' "
+                                           "bf16 autocast with fp32 weights")
+        del lbs, flush
+        torch.cuda.empty_cache()
+        if not args.no_train:
+            extra["train_step"] = _train_step_entry(args, rank, world, dev)
 
     if rank != 0:
         return
-    peak, peak_kind = _peaks()
     step_ms = total_ms / args.steps
     value = world * t * args.steps / (total_ms / 1e3)
     pre_avg = sum(pre_ms) / len(pre_ms)
@@ -462,9 +534,17 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_cpu_baseline:
         times = _cpu_reference(n, c, args.cpu_tokens, args.cpu_budget, 2, 50)
         cpu = {"value": args.cpu_tokens / statistics.median(times), "unit": "tokens/s",
-               "cores": torch.get_num_threads(), "kind": "port",
+               "cores": torch.get_num_threads(), "kind": "port", "cpu_model": _cpu_model(),
                "sample": f"{args.cpu_tokens} tokens x {len(times)} runs (median), C=768, n=4, fp32, "
                          f"f=identity, 20 Sinkhorn iters; oracle restatement of _forward_ref"}
+        # [2, 512, 4, 512] fp32 on the CPU, and the config-2
+        # shape in bf16 (bounded samples)
+        t1 = _cpu_reference(4, 512, 1024, 3.0, 2, 20)
+        cpu["config1_fp32"] = {"value": 1024 / statistics.median(t1), "unit": "tokens/s",
+                               "sample": f"[2,512,4,512] fp32 x {len(t1)} runs (median)"}
+        tb = _cpu_reference(n, c, 1024, 5.0, 2, 10, dtype=torch.bfloat16)
+        cpu["config2_bf16"] = {"value": 1024 / statistics.median(tb), "unit": "tokens/s",
+                               "sample": f"1024 tokens, C=768, n=4, bf16 x {len(tb)} runs (median)"}
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -483,11 +563,14 @@ def run_ours(args, rank, world, local_rank):
         "hbm_frac_of_measured": layer_gbs / peak,
         "algorithmic_bytes_per_token": bytes_tok,
         "per_call_ms": {"pre (coef+sinkhorn+aggregate)": pre_avg, "post (merge)": post_avg},
-        "pre_path": "fused sm_100a cluster kernel (TMA + tcgen05 + DSMEM)" if fused else "generic CUDA-core kernels",
+        "pre_path": {2: "single-read sm_100a cluster kernel (TMA + tcgen05 + TMEM retention + DSMEM)",
+                     1: "two-read sm_100a cluster kernel (TMA + tcgen05 + DSMEM, second read from L2)",
+                     0: "generic CUDA-core kernels"}[fused_path],
+        "pre_two_read": two_read,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic[0] if traffic else None,
-                     "traffic_source": traffic[1] if traffic else None,
+                     "traffic_kind": traffic[1] if traffic else None,
                      "algorithmic_bytes_per_launch": d_bytes},
         "cpu_baseline": cpu,
         "backward": bwd,
@@ -495,7 +578,153 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    line.update(extra)
     print(json.dumps(line), flush=True)
+
+
+def _e2e(lb, args, world, dev, stream, barrier):
+    nat, L = lb.nat, lb.L
+    n, c, t, with_res, iters, fd = lb.n, lb.c, lb.t, lb.with_res, lb.iters, lb.fd
+    ps = lb.ps
+    a_res, b_res = (ps[5], ps[6]) if with_res else (None, None)
+    E2E_CHUNKS, E2E_STREAMS = 8, 3
+    x_h = lb.x.cpu().pin_memory()
+    f_h = lb.f.cpu().pin_memory()
+    o_h = torch.empty_like(x_h).pin_memory()
+    bounds = [t * i // E2E_CHUNKS for i in range(E2E_CHUNKS + 1)]
+    cmax = max(bounds[i + 1] - bounds[i] for i in range(E2E_CHUNKS))
+    streams = [torch.cuda.Stream(dev) for _ in range(E2E_STREAMS)]
+    slots = []
+    for _ in range(E2E_STREAMS):
+        slots.append(dict(
+            x=torch.empty(cmax, n * c, device=dev, dtype=torch.bfloat16),
+            f=torch.empty(cmax, c, device=dev, dtype=torch.bfloat16),
+            o=torch.empty(cmax, n * c, device=dev, dtype=torch.bfloat16),
+            z=torch.empty(cmax, c, device=dev, dtype=torch.bfloat16),
+            hp=torch.empty(cmax, n, device=dev), hr=torch.empty(cmax, n, n, device=dev) if with_res else None,
+            inv=torch.empty(cmax, device=dev), mix=torch.empty(cmax, fd, device=dev),
+            ws=nat.workspace(L.mhc_pre_fwd_workspace(cmax, n, c, int(with_res)), dev)))
+
+    def chunk(k, kernels):
+        lo, hi = bounds[k], bounds[k + 1]
+        m = hi - lo
+        st = streams[k % E2E_STREAMS]
+        sl = slots[k % E2E_STREAMS]
+        sp = st.cuda_stream
+        with torch.cuda.stream(st):
+            sl["x"][:m].copy_(x_h[lo:hi], non_blocking=True)
+            sl["f"][:m].copy_(f_h[lo:hi], non_blocking=True)
+        if kernels:
+            r = L.mhc_pre_fwd(nat.ptr(sl["x"]), nat.BF16, m, n, c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]),
+                              nat.ptr(ps[3]), nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32,
+                              int(with_res), int(with_res), iters, 2.0, 1e-6, 1e-6, 1e-6, nat.ptr(sl["z"]), None,
+                              nat.ptr(sl["hp"]), nat.ptr(sl["hr"]), nat.F32, nat.ptr(sl["inv"]), nat.ptr(sl["mix"]),
+                              nat.ptr(sl["ws"]), sl["ws"].numel(), sp)
+            nat.check(r, "mhc_pre_fwd")
+            r = L.mhc_post_fwd(nat.ptr(sl["x"]), nat.BF16, nat.ptr(sl["hr"]), nat.F32, nat.ptr(sl["hp"]), nat.F32,
+                               nat.ptr(sl["f"]), nat.BF16, nat.ptr(sl["o"]), m, n, c, 0, 0, 0.0, None, sp)
+            nat.check(r, "mhc_post_fwd")
+        with torch.cuda.stream(st):
+            o_h[lo:hi].copy_(sl["o"][:m], non_blocking=True)
+
+    def e2e_step(kernels=True):
+        go = torch.cuda.Event()
+        go.record(stream)
+        for st in streams:
+            st.wait_event(go)
+        for k in range(E2E_CHUNKS):
+            chunk(k, kernels)
+        for st in streams:
+            done = torch.cuda.Event()
+            done.record(st)
+            stream.wait_event(done)
+
+    def timed(kernels, k_steps):
+        for _ in range(max(1, args.warmup)):
+            e2e_step(kernels)
+        barrier()
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(k_steps):
+            e2e_step(kernels)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return _max_over_ranks(s0.elapsed_time(s1), world, dev)
+
+    k_e2e = max(1, min(args.steps, 5))
+    copy_ms = timed(False, k_e2e)
+    e_ms = timed(True, k_e2e)
+    # check every copied-back chunk against the device-side step's result
+    lb.pre()
+    lb.post()
+    torch.cuda.synchronize(dev)
+    e2e_ok = bool(torch.equal(o_h.to(dev), lb.out))
+    value = world * t * k_e2e / (e_ms / 1e3)
+    ceiling = world * t * k_e2e / (copy_ms / 1e3)
+    return {"value": value, "unit": "tokens/s",
+            "h2d_bytes_per_step": int(x_h.numel() * 2 + f_h.numel() * 2),
+            "d2h_bytes_per_step": int(o_h.numel() * 2), "steps": k_e2e, "ms_per_step": e_ms / k_e2e,
+            "pipeline": f"{E2E_CHUNKS} token chunks over {E2E_STREAMS} streams (H2D / kernels / D2H overlap)",
+            "result_matches_device_step": e2e_ok,
+            "host_link_ceiling": {"tokens_per_s": ceiling, "ms_per_step": copy_ms / k_e2e,
+                                  "note": "the same pinned H2D + D2H copies without the kernels, all ranks at once"},
+            "frac_of_host_link_ceiling": value / ceiling}
+
+
+def _train_step_entry(args, rank, world, dev):
+    """BASELINE configs[4] inside the default line: the MoE + mHC training step
+    at 8 x 2048 tokens per GPU (global 64 x 2048 at 8 GPUs), with the gradient
+    all-reduce timed on its own."""
+    import torch.nn.functional as F
+    torch.manual_seed(1234 + rank)
+    model = _build_decoder(moe=True, dev=dev)
+    batch, seq = 8, 2048
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    ids = torch.randint(0, 6400, (batch, seq), device=dev, generator=gen)
+    labels = torch.randint(0, 6400, (batch, seq), device=dev, generator=gen)
+    params = list(model.parameters())
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    stream = torch.cuda.current_stream(dev)
+    ar = []
+
+    def step(timed):
+        logits = model(ids)
+        loss = F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), labels.view(-1)) + model.aux_loss()
+        loss.backward()
+        if world > 1:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            allreduce_grads(params, world)
+            e1.record(stream)
+            if timed:
+                ar.append((e0, e1))
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    for _ in range(3):
+        step(False)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    k = 5
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(k):
+        step(True)
+    s1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = _max_over_ranks(s0.elapsed_time(s1) / k, world, dev)
+    ar_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in ar) / k, world, dev) if ar else 0.0
+    del model, opt
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": world * batch * seq / (ms / 1e3), "ms_per_step": ms, "tokens_per_gpu": batch * seq,
+            "global_batch": f"{world * batch} x {seq}", "allreduce_ms_per_step": ar_ms,
+            "allreduce_share": ar_ms / ms if ms else 0.0,
+            "model": "MiniMind MoE (8 experts, top-2) + mHC on every sublayer: hidden 768, 8 layers, vocab 6400, "
+                     "n=4, 20 Sinkhorn iterations; fwd + bwd + gradient all-reduce + AdamW"}
 
 
 # ---------------------------------------------------------------------------
@@ -794,6 +1023,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-bwd", action="store_true", help="skip the backward measurement")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the token sweep, config-3 and fp32-stream sub-measurements")
+    ap.add_argument("--no-train", action="store_true", help="skip the config-5 training-step sub-measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -245,28 +245,36 @@ int mhc_device_sm_count(void);
 
 /*
  * Kernel selection for mhc_pre_fwd / mhc_head_fwd.  MHC_PATH_AUTO (default)
- * uses the fused sm_100a cluster kernel (TMA + tcgen05 + DSMEM) whenever the
- * call is eligible (bf16 activations, n*C a multiple of 512, C a multiple of
- * 64, n <= 4 for the full layer, n <= 8 otherwise) and the generic CUDA-core
- * kernels otherwise; MHC_PATH_GENERIC forces the generic kernels.  Process-wide;
- * returns the previous policy.  No reference counterpart (reference selected
+ * uses, in this order of preference, the single-read sm_100a kernel (bf16
+ * activations, n in {2, 4}, C a multiple of 128 with 512 <= C <= 1024: x is
+ * read from HBM once), the two-read sm_100a cluster kernel (bf16, n*C a
+ * multiple of 512, C a multiple of 64, n <= 4 for the full layer, n <= 8
+ * otherwise: x read from HBM, then again from L2), else the generic CUDA-core
+ * kernels.  MHC_PATH_TWO_READ skips the single-read kernel; MHC_PATH_GENERIC
+ * forces the generic kernels (forward and backward).  Process-wide; returns
+ * the previous policy.  No reference counterpart (the reference selected
  * Triton kernels through environment flags, model/mhc_common.py:25-29).
  */
-#define MHC_PATH_AUTO    0
-#define MHC_PATH_GENERIC 1
+#define MHC_PATH_AUTO     0
+#define MHC_PATH_GENERIC  1
+#define MHC_PATH_TWO_READ 2
 int mhc_set_path_policy(int policy);
 
-/* 1 if the last mhc_pre_fwd / mhc_head_fwd of the calling thread ran the fused
- * sm_100a kernel, or its last mhc_pre_bwd / mhc_head_bwd ran the tensor-core
- * dx / dphi kernel; 0 if it ran the generic kernels. */
+/* Kernel the process's last mhc_pre_fwd / mhc_head_fwd ran (on any thread:
+ * autograd runs backward on a thread of its own): 2 the single-read sm_100a
+ * kernel, 1 the two-read sm_100a kernel, 0 the generic kernels; after
+ * mhc_pre_bwd / mhc_head_bwd: 1 if the tensor-core dx / dphi kernel ran, 0
+ * for the generic kernels. */
 int mhc_last_path(void);
 
 /*
  * First error code recorded by a fused kernel on the current device (0 = none;
  * 1..6 = a bounded wait of the producer / MMA / row / coefficient /
- * pre-aggregate / Sinkhorn role of the forward kernel ran out, 11..14 = one of
- * the producer / MMA / epilogue / prep roles of the backward tensor-core
- * kernel, 99 = the self-test below).  A kernel whose wait runs out gives up
+ * pre-aggregate / Sinkhorn role of the two-read forward kernel ran out,
+ * 21..26 = the producer / MMA / ingest / coefficient / Sinkhorn / z role of
+ * the single-read forward kernel, 11..14 = one of the producer / MMA /
+ * epilogue / prep roles of the backward tensor-core kernel, 99 = the
+ * self-test below).  A kernel whose wait runs out gives up
  * instead of hanging and overwrites the outputs it owns with NaN.
  * Synchronises the device.  clear != 0 resets the word.  No reference
  * counterpart.

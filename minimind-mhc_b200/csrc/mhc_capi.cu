@@ -54,7 +54,9 @@ static int check_shape(int64_t T, int n, int C) {
 }
 
 static int g_policy = MHC_PATH_AUTO;
-static thread_local int g_last_path = 0;
+// kernel family of the last pre-stage call in the process (the autograd
+// engine runs backward on its own thread, so this is not thread-local)
+static std::atomic<int> g_last_path{0};
 
 // Pinned host word the fused kernels also write their give-up code into
 // (mhc_set_error_flag); null until a caller registers one.
@@ -86,19 +88,21 @@ int mhc_device_sm_count(void) { return device_sm_count(); }
 
 int mhc_set_path_policy(int policy) {
   const int prev = g_policy;
-  if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC) g_policy = policy;
+  if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC || policy == MHC_PATH_TWO_READ) g_policy = policy;
   return prev;
 }
 
-int mhc_last_path(void) { return g_last_path; }
+int mhc_last_path(void) { return g_last_path.load(); }
 
 int mhc_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  const int fwd = read_tc_error(clear != 0);
-  const int bwd = read_tcb_error(clear != 0);
-  const int st = read_selftest_error(clear != 0);
-  if (fwd < 0 || bwd < 0 || st < 0) return -1;
-  return fwd != 0 ? fwd : (bwd != 0 ? bwd : st);
+  const int words[4] = {read_sr_error(clear != 0), read_tc_error(clear != 0), read_tcb_error(clear != 0),
+                        read_selftest_error(clear != 0)};
+  for (int w : words)
+    if (w < 0) return -1;
+  for (int w : words)
+    if (w != 0) return w;
+  return 0;
 }
 
 int mhc_set_error_flag(int *host_flag) {
@@ -159,7 +163,17 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
   float *gate = reinterpret_cast<float *>(workspace);
   const int mode = with_res ? 0 : 1;
   g_last_path = 0;
-  if (g_policy == MHC_PATH_AUTO && pre_tc_eligible(mode, n, x_dtype, x, z, T, C)) {
+  if (g_policy == MHC_PATH_AUTO && pre_sr_eligible(mode, n, x_dtype, x, z, T, C)) {
+    cudaError_t e = launch_pre_sr(mode, n, x, T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr,
+                                  coef_dtype, inv_rms, mixes, s);
+    if (e == cudaSuccess) {
+      g_last_path = 2;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_pre_fwd single-read");
+    cudaGetLastError();  // not supported on this device: the kernels below
+  }
+  if (g_policy != MHC_PATH_GENERIC && pre_tc_eligible(mode, n, x_dtype, x, z, T, C)) {
     cudaError_t e = launch_pre_tc(mode, n, x, T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr,
                                   coef_dtype, inv_rms, mixes, s);
     if (e == cudaSuccess) {
@@ -256,7 +270,7 @@ static int pre_bwd_common(int mode, const void *x, int x_dtype, int64_t T, int n
   if (!workspace || workspace_bytes < plan.total)
     return fail(MHC_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, plan.total);
   if (!aligned(workspace, 256)) return fail(MHC_ERR_ALIGN, "%s: workspace must be 256-byte aligned", who);
-  const bool use_tc = g_policy == MHC_PATH_AUTO && pre_bwd_tc_eligible(mode, n, x_dtype, T, C, x, dz, dx_add, dx);
+  const bool use_tc = g_policy != MHC_PATH_GENERIC && pre_bwd_tc_eligible(mode, n, x_dtype, T, C, x, dz, dx_add, dx);
   g_last_path = use_tc ? 1 : 0;
   return cuda_status(launch_pre_bwd(mode, n, x_dtype, x, T, C, phi, p, inv_rms, mixes, dz, dh_pre,
                                     dh_post, dh_res, coef_dtype, dx_add, dx, dphi, da_pre, db_pre,
@@ -341,7 +355,17 @@ int mhc_head_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void
   CoefParams p{alpha, bias, nullptr, nullptr, nullptr, nullptr, param_dtype, 1.f, pre_eps, rms_eps, 0.f, 0, 0};
   float *gate = reinterpret_cast<float *>(workspace);
   g_last_path = 0;
-  if (g_policy == MHC_PATH_AUTO && pre_tc_eligible(2, n, x_dtype, x, out, T, C)) {
+  if (g_policy == MHC_PATH_AUTO && pre_sr_eligible(2, n, x_dtype, x, out, T, C)) {
+    cudaError_t e = launch_pre_sr(2, n, x, T, C, phi, p, out, nullptr, nullptr, nullptr, MHC_F32, inv_rms,
+                                  mix_raw, s);
+    if (e == cudaSuccess) {
+      g_last_path = 2;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_head_fwd single-read");
+    cudaGetLastError();
+  }
+  if (g_policy != MHC_PATH_GENERIC && pre_tc_eligible(2, n, x_dtype, x, out, T, C)) {
     cudaError_t e = launch_pre_tc(2, n, x, T, C, phi, p, out, nullptr, nullptr, nullptr, MHC_F32, inv_rms,
                                   mix_raw, s);
     if (e == cudaSuccess) {

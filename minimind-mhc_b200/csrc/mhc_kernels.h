@@ -47,6 +47,14 @@ cudaError_t launch_pre_tc(int mode, int n, const void *x, int64_t T, int C, cons
                           int coef_dtype, float *inv_rms, float *mixes, cudaStream_t stream);
 int read_tc_error(bool clear);
 
+// ---- single-read sm_100a coefficient + pre-aggregate (bf16 activations) ----
+// n in {2, 4}, C a multiple of 128 with 4 <= C / 128 <= 8
+bool pre_sr_eligible(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C);
+cudaError_t launch_pre_sr(int mode, int n, const void *x, int64_t T, int C, const void *phi,
+                          const CoefParams &p, void *z, void *h_pre, void *h_post, void *h_res,
+                          int coef_dtype, float *inv_rms, float *mixes, cudaStream_t stream);
+int read_sr_error(bool clear);
+
 cudaError_t launch_post_bwd(int n, int x_dtype, const void *dout, const void *x, const void *h_res,
                             int h_res_dtype, const void *h_post, int h_post_dtype, const void *f,
                             int f_dtype, void *dx, void *dh_res, void *dh_post, void *df,

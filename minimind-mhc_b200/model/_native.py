@@ -59,7 +59,7 @@ _PROTOS = {
                                  _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P]),
 }
 
-PATH_AUTO, PATH_GENERIC = 0, 1
+PATH_AUTO, PATH_GENERIC, PATH_TWO_READ = 0, 1, 2
 
 EXPORTED = tuple(_PROTOS)
 
@@ -140,7 +140,10 @@ def workspace(nbytes: int, device) -> torch.Tensor:
 ERROR_ROLES = {1: "forward TMA producer", 2: "forward MMA issuer", 3: "forward row warps",
                4: "forward coefficient warp", 5: "forward pre-aggregate warps", 6: "forward Sinkhorn warp",
                11: "backward TMA producer", 12: "backward MMA issuer", 13: "backward epilogue",
-               14: "backward prep warps", 99: "bounded-wait self-test"}
+               14: "backward prep warps", 21: "single-read forward TMA producer",
+               22: "single-read forward MMA issuer", 23: "single-read forward ingest warps",
+               24: "single-read forward coefficient warp", 25: "single-read forward Sinkhorn warps",
+               26: "single-read forward z warps", 99: "bounded-wait self-test"}
 
 _flag_tensor = None   # pinned int32 host tensor registered with the library
 _flag_word = None     # ctypes view of its first element

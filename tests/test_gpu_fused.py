@@ -1,11 +1,15 @@
-"""Fused sm_100a coefficient kernel (TMA + tcgen05 + DSMEM cluster) vs the
-generic CUDA-core kernels and the oracle.
+"""The fused sm_100a coefficient kernels vs the generic CUDA-core kernels and
+the oracle.
 
-Both paths compute the same fp32 coefficient math; the fused kernel's
-projection runs on the tensor cores with phi split into bf16 hi + lo halves
-(relative error ~2^-17), so coefficients agree to 2e-5 relative and the bf16
+Two fused kernels compute the forward coefficient stage for bf16 activations:
+the single-read kernel (x read from HBM once, TMEM-retained chunks, policy
+AUTO where eligible) and the two-read kernel (x read from HBM, then from L2;
+policy TWO_READ, and AUTO where the single-read kernel does not apply).  Both
+compute the same fp32 coefficient math as the generic kernels; the projection
+runs on the tensor cores with phi split into bf16 hi + lo halves (relative
+error ~2^-17), so coefficients agree to 2e-5 relative and the bf16
 pre-aggregate z to one bf16 rounding.  Every run also checks the device error
-word of the fused kernel (a bounded wait that ran out would set it).
+words (a bounded wait that ran out would set one).
 """
 
 import pytest
@@ -16,11 +20,31 @@ from oracle import mhc_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
+AUTO, GENERIC, TWO_READ = 0, 1, 2
 
 
 def _lib():
     from model import _native as nat
     return nat, nat.lib()
+
+
+def _sr_ok(n, c, mode="full"):
+    return n in (2, 4) and c % 128 == 0 and 4 <= c // 128 <= 8
+
+
+def _tc_ok(n, c, mode="full"):
+    nc = n * c
+    if nc % 512 or c % 64 or nc // 512 > 8 or c // 8 > 256:
+        return False
+    return n <= 4 if mode == "full" else n <= 8
+
+
+def expected_path(n, c, policy, mode="full"):
+    if policy == AUTO and _sr_ok(n, c, mode):
+        return 2
+    if policy != GENERIC and _tc_ok(n, c, mode):
+        return 1
+    return 0
 
 
 def _run_pre(x, ps, with_res, n, c, policy, apply_sk=False, iters=20):
@@ -59,18 +83,25 @@ CASES = [
     (8, 512, 260, False),
     (2, 768, 515, False),
     (4, 768, 16 * 128 * 15 + 3, True),  # every cluster busy, a partial last tile
+    (4, 640, 300, True),       # 5-CTA clusters in the single-read kernel
+    (4, 896, 257, False),      # 7-CTA clusters
+    (4, 768, 24 * 128 * 3 + 64, False),  # several tiles per cluster, a half tile
 ]
 
 
+@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["auto", "two_read"])
 @pytest.mark.parametrize("n,c,t,with_res", CASES)
-def test_fused_matches_generic_and_oracle(n, c, t, with_res):
+def test_fused_matches_generic_and_oracle(n, c, t, with_res, policy):
+    want = expected_path(n, c, policy, "full" if with_res else "nohres")
+    if want == 0 or (policy == TWO_READ and want == expected_path(n, c, AUTO)):
+        pytest.skip("no distinct fused kernel for this shape and policy")
     gen = torch.Generator().manual_seed(n * 100 + t)
     ps, raw = _params(n, c, with_res, gen)
     x = torch.randn(t, n * c, generator=gen).bfloat16()
     xd = x.to(DEV)
-    (zf, hpf, hof, hrf, invf, mixf), path_f = _run_pre(xd, ps, with_res, n, c, 0)
-    (zg, hpg, hog, hrg, invg, mixg), path_g = _run_pre(xd, ps, with_res, n, c, 1)
-    assert path_f == 1, "fused sm_100a kernel did not run on an eligible shape"
+    (zf, hpf, hof, hrf, invf, mixf), path_f = _run_pre(xd, ps, with_res, n, c, policy)
+    (zg, hpg, hog, hrg, invg, mixg), path_g = _run_pre(xd, ps, with_res, n, c, GENERIC)
+    assert path_f == want, "the expected fused sm_100a kernel did not run"
     assert path_g == 0
     assert max_rel(invg, invf) < 1e-5
     assert max_rel(mixg, mixf) < 2e-5
@@ -95,9 +126,12 @@ def test_fused_sinkhorn_matches_merge_kernel_sinkhorn():
     n, c, t = 4, 768, 1024
     ps, _ = _params(n, c, True, gen)
     xd = torch.randn(t, n * c, generator=gen).bfloat16().to(DEV)
-    (z, _, hpost, hres_norm, _, _), path = _run_pre(xd, ps, True, n, c, 0, apply_sk=True)
-    assert path == 1
-    (_, _, _, hres_logit, _, _), _ = _run_pre(xd, ps, True, n, c, 0, apply_sk=False)
+    (z, _, hpost, hres_norm, _, _), path = _run_pre(xd, ps, True, n, c, AUTO, apply_sk=True)
+    assert path == 2
+    (_, _, _, hres_logit, _, _), _ = _run_pre(xd, ps, True, n, c, AUTO, apply_sk=False)
+    (_, _, _, hres_norm_tr, _, _), path_tr = _run_pre(xd, ps, True, n, c, TWO_READ, apply_sk=True)
+    assert path_tr == 1
+    assert max_rel(hres_norm_tr, hres_norm) < 1e-5
     ref = O.sinkhorn(hres_logit.cpu(), 20, 1e-6)
     assert max_rel(ref, hres_norm) < 1e-5
     f = torch.randn(t, c, generator=gen).bfloat16().to(DEV)
@@ -114,7 +148,8 @@ def test_fused_sinkhorn_matches_merge_kernel_sinkhorn():
     assert (out1.float() - out2.float()).abs().max().item() <= 2 ** -7 * out1.float().abs().max().item()
 
 
-def test_fused_full_size_repeatable():
+@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["single_read", "two_read"])
+def test_fused_full_size_repeatable(policy):
     """32768 tokens (the benchmark batch) twice: bit-identical outputs, no
     device error, and sampled tokens against the generic path."""
     gen = torch.Generator().manual_seed(11)
@@ -122,9 +157,9 @@ def test_fused_full_size_repeatable():
     ps, _ = _params(n, c, True, gen)
     torch.manual_seed(5)
     xd = torch.randn(t, n * c, device=DEV).bfloat16()
-    (z1, _, ho1, hr1, inv1, mix1), p1 = _run_pre(xd, ps, True, n, c, 0)
-    (z2, _, ho2, hr2, inv2, mix2), p2 = _run_pre(xd, ps, True, n, c, 0)
-    assert p1 == 1 and p2 == 1
+    (z1, _, ho1, hr1, inv1, mix1), p1 = _run_pre(xd, ps, True, n, c, policy)
+    (z2, _, ho2, hr2, inv2, mix2), p2 = _run_pre(xd, ps, True, n, c, policy)
+    assert p1 == p2 == expected_path(n, c, policy)
     for a, b in [(z1, z2), (ho1, ho2), (hr1, hr2), (inv1, inv2), (mix1, mix2)]:
         assert torch.equal(a, b)
     idx = torch.randperm(t, generator=gen)[:2048].to(DEV)
@@ -134,19 +169,20 @@ def test_fused_full_size_repeatable():
     assert (zg.float() - z1[idx].float()).abs().max().item() <= 2 ** -7 * zg.float().abs().max().item()
 
 
-def test_fused_head_matches_generic():
+@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["single_read", "two_read"])
+def test_fused_head_matches_generic(policy):
     nat, L = _lib()
     from model.mhc_common import MHCHead
     torch.manual_seed(3)
     n, c, t = 4, 768, 600
     head = MHCHead(n, c).to(DEV)
     x = torch.randn(1, t, n * c, device=DEV).bfloat16()
-    prev = L.mhc_set_path_policy(0)
+    prev = L.mhc_set_path_policy(policy)
     y_f = head(x)
     path = L.mhc_last_path()
-    L.mhc_set_path_policy(1)
+    L.mhc_set_path_policy(GENERIC)
     y_g = head(x)
     L.mhc_set_path_policy(prev)
-    assert path == 1
+    assert path == expected_path(n, c, policy, "head")
     assert L.mhc_device_error(1) == 0
     assert (y_g.float() - y_f.float()).abs().max().item() <= 2 ** -7 * y_g.float().abs().max().item()

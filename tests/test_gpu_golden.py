@@ -82,7 +82,7 @@ def _module_case(g, mod, k):
     from model import _native as nat
     y = mod(x, fn)
     if k.endswith("_wide"):
-        assert nat.lib().mhc_last_path() == 1, "the fused sm_100a forward did not run"
+        assert nat.lib().mhc_last_path() >= 1, "a fused sm_100a forward did not run"
     assert_close(k + ".out", g["out"], y, atol, rtol)
     loss = y.float().pow(2).mean()
     ps = [p for _, p in mod.named_parameters()]
