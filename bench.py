@@ -15,7 +15,7 @@ device synchronise, CUDA events on the launching stream, max over ranks.  x is
 
 The same JSON line also carries, measured in the same run:
   * "backward": the layer backward (merge backward + coefficient backward);
-  * "pre_two_read": the previous fused forward kernel on the same inputs;
+  * "pre_other_kernel": the other fused forward kernel on the same inputs;
   * "e2e": the layer through the C-ABI from pinned host buffers, with the
     host link's copy-only ceiling;
   * "sweep": configs[1]'s token sweep, 4K to 256K tokens per GPU (L2 flushed
@@ -385,7 +385,15 @@ def _layer_entry(lb, world, dev, steps, warmup, stream, peak, flush, with_bwd, s
     f_ms = _max_over_ranks(f_ms, world, dev)
     n, c, t = lb.n, lb.c, lb.t
     fb = _fwd_bytes(n, c, sx, sf)
+    alt_pre = None
+    if lb.pre_path == 1 and sx == 2:
+        prev = lb.L.mhc_set_path_policy(lb.nat.PATH_SINGLE_READ)
+        _, (p_ms,) = _time_steps([lb.pre], steps, warmup, stream, fl)
+        if lb.L.mhc_last_path() == 2:
+            alt_pre = p_ms
+        lb.L.mhc_set_path_policy(prev)
     e = {"tokens_per_gpu": t, "tokens_per_s": world * t / (f_ms / 1e3), "ms_per_step": f_ms,
+         "pre_single_read_ms": alt_pre,
          "algorithmic_bytes_per_token": fb, "hbm_gbs_per_gpu": fb * t / (f_ms / 1e3) / 1e9,
          "frac_of_measured": fb * t / (f_ms / 1e3) / 1e9 / peak,
          "per_call_ms": {"pre": pre_ms, "post": post_ms}, "pre_path": lb.pre_path,
@@ -458,15 +466,19 @@ def run_ours(args, rank, world, local_rank):
     pre_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev]
     post_ms = [e1.elapsed_time(e2) for _, e1, e2 in ev]
 
-    # ---- the two-read fused kernel on the same inputs, for comparison ---------
-    two_read = None
-    if fused_path == 2:
-        prev = L.mhc_set_path_policy(nat.PATH_TWO_READ)
-        tr_ms, (tr_pre,) = _time_steps([lb.pre], max(10, args.steps // 4), 3, stream)
-        two_read = {"pre_ms": tr_pre, "path": L.mhc_last_path(),
-                    "note": "x read from HBM by TMA, then again from L2 (the previous design)"}
+    # ---- the other fused forward kernel on the same inputs, for comparison -----
+    alt = None
+    if fused_path in (1, 2):
+        other = nat.PATH_SINGLE_READ if fused_path == 1 else nat.PATH_TWO_READ
+        prev = L.mhc_set_path_policy(other)
+        _, (alt_pre,) = _time_steps([lb.pre], max(10, args.steps // 4), 3, stream)
+        alt_path = L.mhc_last_path()
         L.mhc_set_path_policy(prev)
         lb.pre()
+        if alt_path != fused_path:
+            alt = {"pre_ms": alt_pre, "path": alt_path,
+                   "kernel": {2: "single-read (x read from HBM once, kept in TMEM)",
+                              1: "two-read (x read from HBM, then again from L2)"}.get(alt_path, "generic")}
 
     # ---- backward of the layer (training config), reported beside the forward --
     bwd = None
@@ -566,7 +578,7 @@ def run_ours(args, rank, world, local_rank):
         "pre_path": {2: "single-read sm_100a cluster kernel (TMA + tcgen05 + TMEM retention + DSMEM)",
                      1: "two-read sm_100a cluster kernel (TMA + tcgen05 + DSMEM, second read from L2)",
                      0: "generic CUDA-core kernels"}[fused_path],
-        "pre_two_read": two_read,
+        "pre_other_kernel": alt,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": traffic[0] if traffic else None,

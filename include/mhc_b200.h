@@ -244,20 +244,25 @@ int mhc_stream_expand_bwd(const void *dout, void *dx, int dtype, int64_t T, int 
 int mhc_device_sm_count(void);
 
 /*
- * Kernel selection for mhc_pre_fwd / mhc_head_fwd.  MHC_PATH_AUTO (default)
- * uses, in this order of preference, the single-read sm_100a kernel (bf16
- * activations, n in {2, 4}, C a multiple of 128 with 512 <= C <= 1024: x is
- * read from HBM once), the two-read sm_100a cluster kernel (bf16, n*C a
- * multiple of 512, C a multiple of 64, n <= 4 for the full layer, n <= 8
- * otherwise: x read from HBM, then again from L2), else the generic CUDA-core
- * kernels.  MHC_PATH_TWO_READ skips the single-read kernel; MHC_PATH_GENERIC
- * forces the generic kernels (forward and backward).  Process-wide; returns
- * the previous policy.  No reference counterpart (the reference selected
- * Triton kernels through environment flags, model/mhc_common.py:25-29).
+ * Kernel selection for mhc_pre_fwd / mhc_head_fwd.  Two sm_100a kernels
+ * compute the forward coefficient stage for bf16 activations: the two-read
+ * cluster kernel (n*C a multiple of 512, C a multiple of 64, n <= 4 for the
+ * full layer, n <= 8 otherwise; x read from HBM, then again from L2) and the
+ * single-read kernel (n in {2, 4}, C a multiple of 128 with 512 <= C <= 1024;
+ * x read from HBM once and kept in TMEM).  MHC_PATH_AUTO (default) picks the
+ * faster of the two for the call, as measured on B200: the single-read kernel
+ * for the no-H_res and head layers and for full layers of fewer than 32,768
+ * tokens, the two-read kernel for longer full-layer batches; then the generic
+ * CUDA-core kernels.  MHC_PATH_SINGLE_READ prefers the single-read kernel;
+ * MHC_PATH_TWO_READ never uses it; MHC_PATH_GENERIC forces the generic
+ * kernels (forward and backward).  Process-wide; returns the previous policy.
+ * No reference counterpart (the reference selected Triton kernels through
+ * environment flags, model/mhc_common.py:25-29).
  */
-#define MHC_PATH_AUTO     0
-#define MHC_PATH_GENERIC  1
-#define MHC_PATH_TWO_READ 2
+#define MHC_PATH_AUTO        0
+#define MHC_PATH_GENERIC     1
+#define MHC_PATH_TWO_READ    2
+#define MHC_PATH_SINGLE_READ 3
 int mhc_set_path_policy(int policy);
 
 /* Kernel the process's last mhc_pre_fwd / mhc_head_fwd ran (on any thread:

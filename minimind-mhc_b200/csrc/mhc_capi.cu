@@ -63,6 +63,20 @@ static std::atomic<int> g_last_path{0};
 static std::atomic<int *> g_host_flag{nullptr};
 int *host_error_flag() { return g_host_flag.load(std::memory_order_acquire); }
 
+// Which fused forward kernel MHC_PATH_AUTO runs, from B200 measurements
+// (µs per call, two-read / single-read): full layer C=768 at 4K tokens
+// 30.8 / 26.6, 16K 54.3 / 51.6, 32K 83.7 / 84.7, 64K 144 / 151, 256K 512 /
+// 550; no-H_res at 32K tokens C=768 75.9 / 71.2, C=1024 93.5 / 89.3.  The
+// single-read kernel wins when the tile sequence per cluster is short (its
+// per-tile latency chain is hidden less) and for the narrow projections of the
+// no-H_res and head layers; the two-read kernel for long full-layer batches.
+static bool use_single_read(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C) {
+  if (g_policy == MHC_PATH_SINGLE_READ) return pre_sr_eligible(mode, n, x_dtype, x, z, T, C);
+  if (g_policy != MHC_PATH_AUTO || !pre_sr_eligible(mode, n, x_dtype, x, z, T, C)) return false;
+  if (!pre_tc_eligible(mode, n, x_dtype, x, z, T, C)) return true;
+  return mode != 0 || T < 32768;
+}
+
 static int check_elem_align(const void *p, int dtype, const char *name) {
   if (p && !aligned(p, esize(dtype))) return fail(MHC_ERR_ALIGN, "%s is not %zu-byte aligned", name, esize(dtype));
   return MHC_OK;
@@ -88,7 +102,9 @@ int mhc_device_sm_count(void) { return device_sm_count(); }
 
 int mhc_set_path_policy(int policy) {
   const int prev = g_policy;
-  if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC || policy == MHC_PATH_TWO_READ) g_policy = policy;
+  if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC || policy == MHC_PATH_TWO_READ ||
+      policy == MHC_PATH_SINGLE_READ)
+    g_policy = policy;
   return prev;
 }
 
@@ -163,7 +179,7 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
   float *gate = reinterpret_cast<float *>(workspace);
   const int mode = with_res ? 0 : 1;
   g_last_path = 0;
-  if (g_policy == MHC_PATH_AUTO && pre_sr_eligible(mode, n, x_dtype, x, z, T, C)) {
+  if (use_single_read(mode, n, x_dtype, x, z, T, C)) {
     cudaError_t e = launch_pre_sr(mode, n, x, T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr,
                                   coef_dtype, inv_rms, mixes, s);
     if (e == cudaSuccess) {
@@ -355,7 +371,7 @@ int mhc_head_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void
   CoefParams p{alpha, bias, nullptr, nullptr, nullptr, nullptr, param_dtype, 1.f, pre_eps, rms_eps, 0.f, 0, 0};
   float *gate = reinterpret_cast<float *>(workspace);
   g_last_path = 0;
-  if (g_policy == MHC_PATH_AUTO && pre_sr_eligible(2, n, x_dtype, x, out, T, C)) {
+  if (use_single_read(2, n, x_dtype, x, out, T, C)) {
     cudaError_t e = launch_pre_sr(2, n, x, T, C, phi, p, out, nullptr, nullptr, nullptr, MHC_F32, inv_rms,
                                   mix_raw, s);
     if (e == cudaSuccess) {

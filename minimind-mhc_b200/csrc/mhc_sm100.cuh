@@ -63,6 +63,26 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
       : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
 }
+// Non-blocking probes of the same (no suspension): the fast path of a wait
+// whose phase has usually completed already.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
 
 // Bounded wait.  Returns false after `limit` clock cycles or as soon as
 // *abort (if given) becomes non-zero.
@@ -81,6 +101,14 @@ __device__ __forceinline__ bool wait_parity_limit(uint32_t bar, uint32_t parity,
 // The wait every kernel uses: bounded by MHC_WAIT_CYCLES (about one second).
 template <bool CLUSTER>
 __device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, const volatile int *abort) {
+  return wait_parity_limit<CLUSTER>(bar, parity, abort, MHC_WAIT_CYCLES);
+}
+
+// The same with a non-blocking probe first, for waits that are mostly
+// satisfied already when they are reached.
+template <bool CLUSTER>
+__device__ __forceinline__ bool wait_parity_fast(uint32_t bar, uint32_t parity, const volatile int *abort) {
+  if (CLUSTER ? mbar_test_wait_cluster(bar, parity) : mbar_test_wait(bar, parity)) return true;
   return wait_parity_limit<CLUSTER>(bar, parity, abort, MHC_WAIT_CYCLES);
 }
 
@@ -135,6 +163,12 @@ __device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, flo
                ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
                : "memory");
 }
+// The same for one 4-byte word.
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float a, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(addr), "f"(a),
+               "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -166,6 +200,24 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int 
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing
+// `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// 3-D tiled load of one box into this CTA's shared memory, completing `bar`'s
+// transaction count.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 
@@ -296,6 +348,50 @@ __device__ __forceinline__ void tmem_ld16u(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// Four loads of 16 columns each (column addresses a0..a3) and their wait in
+// one asm statement, so no register is read before the data has landed.
+__device__ __forceinline__ void tmem_ld16x4u(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t (&r)[4][16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%65];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47}, [%66];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%67];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0][0]), "=r"(r[0][1]), "=r"(r[0][2]), "=r"(r[0][3]), "=r"(r[0][4]), "=r"(r[0][5]), "=r"(r[0][6]),
+        "=r"(r[0][7]), "=r"(r[0][8]), "=r"(r[0][9]), "=r"(r[0][10]), "=r"(r[0][11]), "=r"(r[0][12]),
+        "=r"(r[0][13]), "=r"(r[0][14]), "=r"(r[0][15]),
+        "=r"(r[1][0]), "=r"(r[1][1]), "=r"(r[1][2]), "=r"(r[1][3]), "=r"(r[1][4]), "=r"(r[1][5]), "=r"(r[1][6]),
+        "=r"(r[1][7]), "=r"(r[1][8]), "=r"(r[1][9]), "=r"(r[1][10]), "=r"(r[1][11]), "=r"(r[1][12]),
+        "=r"(r[1][13]), "=r"(r[1][14]), "=r"(r[1][15]),
+        "=r"(r[2][0]), "=r"(r[2][1]), "=r"(r[2][2]), "=r"(r[2][3]), "=r"(r[2][4]), "=r"(r[2][5]), "=r"(r[2][6]),
+        "=r"(r[2][7]), "=r"(r[2][8]), "=r"(r[2][9]), "=r"(r[2][10]), "=r"(r[2][11]), "=r"(r[2][12]),
+        "=r"(r[2][13]), "=r"(r[2][14]), "=r"(r[2][15]),
+        "=r"(r[3][0]), "=r"(r[3][1]), "=r"(r[3][2]), "=r"(r[3][3]), "=r"(r[3][4]), "=r"(r[3][5]), "=r"(r[3][6]),
+        "=r"(r[3][7]), "=r"(r[3][8]), "=r"(r[3][9]), "=r"(r[3][10]), "=r"(r[3][11]), "=r"(r[3][12]),
+        "=r"(r[3][13]), "=r"(r[3][14]), "=r"(r[3][15])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3));
+}
+
+// Two loads of 32 columns each (column addresses a0, a1) and their wait in one
+// asm statement.
+__device__ __forceinline__ void tmem_ld32x2u(uint32_t a0, uint32_t a1, uint32_t (&r)[2][32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0][0]), "=r"(r[0][1]), "=r"(r[0][2]), "=r"(r[0][3]), "=r"(r[0][4]), "=r"(r[0][5]), "=r"(r[0][6]), "=r"(r[0][7]), "=r"(r[0][8]), "=r"(r[0][9]), "=r"(r[0][10]), "=r"(r[0][11]), "=r"(r[0][12]), "=r"(r[0][13]), "=r"(r[0][14]), "=r"(r[0][15]), "=r"(r[0][16]), "=r"(r[0][17]), "=r"(r[0][18]), "=r"(r[0][19]), "=r"(r[0][20]), "=r"(r[0][21]), "=r"(r[0][22]), "=r"(r[0][23]), "=r"(r[0][24]), "=r"(r[0][25]), "=r"(r[0][26]), "=r"(r[0][27]), "=r"(r[0][28]), "=r"(r[0][29]), "=r"(r[0][30]), "=r"(r[0][31]), "=r"(r[1][0]), "=r"(r[1][1]), "=r"(r[1][2]), "=r"(r[1][3]), "=r"(r[1][4]), "=r"(r[1][5]), "=r"(r[1][6]), "=r"(r[1][7]), "=r"(r[1][8]), "=r"(r[1][9]), "=r"(r[1][10]), "=r"(r[1][11]), "=r"(r[1][12]), "=r"(r[1][13]), "=r"(r[1][14]), "=r"(r[1][15]), "=r"(r[1][16]), "=r"(r[1][17]), "=r"(r[1][18]), "=r"(r[1][19]), "=r"(r[1][20]), "=r"(r[1][21]), "=r"(r[1][22]), "=r"(r[1][23]), "=r"(r[1][24]), "=r"(r[1][25]), "=r"(r[1][26]), "=r"(r[1][27]), "=r"(r[1][28]), "=r"(r[1][29]), "=r"(r[1][30]), "=r"(r[1][31])
+      : "r"(a0), "r"(a1));
+}
+
+// Asynchronous copy of a 128-row x 32-byte block of a shared-memory matrix
+// (described by a UMMA descriptor, swizzle included) into TMEM lanes 0-127,
+// 8 columns from taddr.  Ordered with the issuing thread's later tcgen05.mma
+// and tracked by its tcgen05.commit.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // 32 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers:

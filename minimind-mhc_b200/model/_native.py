@@ -59,7 +59,7 @@ _PROTOS = {
                                  _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P]),
 }
 
-PATH_AUTO, PATH_GENERIC, PATH_TWO_READ = 0, 1, 2
+PATH_AUTO, PATH_GENERIC, PATH_TWO_READ, PATH_SINGLE_READ = 0, 1, 2, 3
 
 EXPORTED = tuple(_PROTOS)
 

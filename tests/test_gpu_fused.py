@@ -2,9 +2,9 @@
 the oracle.
 
 Two fused kernels compute the forward coefficient stage for bf16 activations:
-the single-read kernel (x read from HBM once, TMEM-retained chunks, policy
-AUTO where eligible) and the two-read kernel (x read from HBM, then from L2;
-policy TWO_READ, and AUTO where the single-read kernel does not apply).  Both
+the two-read kernel (x read from HBM, then from L2; policy AUTO where it
+applies) and the single-read kernel (x read from HBM once, chunks retained in
+TMEM; policy SINGLE_READ, and AUTO where the two-read kernel does not apply).  Both
 compute the same fp32 coefficient math as the generic kernels; the projection
 runs on the tensor cores with phi split into bf16 hi + lo halves (relative
 error ~2^-17), so coefficients agree to 2e-5 relative and the bf16
@@ -20,7 +20,7 @@ from oracle import mhc_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-AUTO, GENERIC, TWO_READ = 0, 1, 2
+AUTO, GENERIC, TWO_READ, SINGLE_READ = 0, 1, 2, 3
 
 
 def _lib():
@@ -39,10 +39,15 @@ def _tc_ok(n, c, mode="full"):
     return n <= 4 if mode == "full" else n <= 8
 
 
-def expected_path(n, c, policy, mode="full"):
-    if policy == AUTO and _sr_ok(n, c, mode):
+def expected_path(n, c, policy, mode="full", t=32768):
+    """The kernel family the C-ABI selects (2 single-read, 1 two-read, 0 generic)."""
+    if policy == GENERIC:
+        return 0
+    if policy == SINGLE_READ and _sr_ok(n, c, mode):
         return 2
-    if policy != GENERIC and _tc_ok(n, c, mode):
+    if policy == AUTO and _sr_ok(n, c, mode) and (not _tc_ok(n, c, mode) or mode != "full" or t < 32768):
+        return 2
+    if _tc_ok(n, c, mode):
         return 1
     return 0
 
@@ -89,12 +94,13 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["auto", "two_read"])
+@pytest.mark.parametrize("policy", [SINGLE_READ, TWO_READ], ids=["single_read", "two_read"])
 @pytest.mark.parametrize("n,c,t,with_res", CASES)
 def test_fused_matches_generic_and_oracle(n, c, t, with_res, policy):
-    want = expected_path(n, c, policy, "full" if with_res else "nohres")
-    if want == 0 or (policy == TWO_READ and want == expected_path(n, c, AUTO)):
-        pytest.skip("no distinct fused kernel for this shape and policy")
+    mode = "full" if with_res else "nohres"
+    want = expected_path(n, c, policy, mode, t)
+    if want == 0 or (policy == SINGLE_READ and want != 2):
+        pytest.skip("this kernel does not apply to the shape")
     gen = torch.Generator().manual_seed(n * 100 + t)
     ps, raw = _params(n, c, with_res, gen)
     x = torch.randn(t, n * c, generator=gen).bfloat16()
@@ -126,9 +132,9 @@ def test_fused_sinkhorn_matches_merge_kernel_sinkhorn():
     n, c, t = 4, 768, 1024
     ps, _ = _params(n, c, True, gen)
     xd = torch.randn(t, n * c, generator=gen).bfloat16().to(DEV)
-    (z, _, hpost, hres_norm, _, _), path = _run_pre(xd, ps, True, n, c, AUTO, apply_sk=True)
+    (z, _, hpost, hres_norm, _, _), path = _run_pre(xd, ps, True, n, c, SINGLE_READ, apply_sk=True)
     assert path == 2
-    (_, _, _, hres_logit, _, _), _ = _run_pre(xd, ps, True, n, c, AUTO, apply_sk=False)
+    (_, _, _, hres_logit, _, _), _ = _run_pre(xd, ps, True, n, c, SINGLE_READ, apply_sk=False)
     (_, _, _, hres_norm_tr, _, _), path_tr = _run_pre(xd, ps, True, n, c, TWO_READ, apply_sk=True)
     assert path_tr == 1
     assert max_rel(hres_norm_tr, hres_norm) < 1e-5
@@ -148,7 +154,7 @@ def test_fused_sinkhorn_matches_merge_kernel_sinkhorn():
     assert (out1.float() - out2.float()).abs().max().item() <= 2 ** -7 * out1.float().abs().max().item()
 
 
-@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["single_read", "two_read"])
+@pytest.mark.parametrize("policy", [SINGLE_READ, TWO_READ], ids=["single_read", "two_read"])
 def test_fused_full_size_repeatable(policy):
     """32768 tokens (the benchmark batch) twice: bit-identical outputs, no
     device error, and sampled tokens against the generic path."""
@@ -159,7 +165,7 @@ def test_fused_full_size_repeatable(policy):
     xd = torch.randn(t, n * c, device=DEV).bfloat16()
     (z1, _, ho1, hr1, inv1, mix1), p1 = _run_pre(xd, ps, True, n, c, policy)
     (z2, _, ho2, hr2, inv2, mix2), p2 = _run_pre(xd, ps, True, n, c, policy)
-    assert p1 == p2 == expected_path(n, c, policy)
+    assert p1 == p2 == expected_path(n, c, policy, "full", t)
     for a, b in [(z1, z2), (ho1, ho2), (hr1, hr2), (inv1, inv2), (mix1, mix2)]:
         assert torch.equal(a, b)
     idx = torch.randperm(t, generator=gen)[:2048].to(DEV)
@@ -169,7 +175,7 @@ def test_fused_full_size_repeatable(policy):
     assert (zg.float() - z1[idx].float()).abs().max().item() <= 2 ** -7 * zg.float().abs().max().item()
 
 
-@pytest.mark.parametrize("policy", [AUTO, TWO_READ], ids=["single_read", "two_read"])
+@pytest.mark.parametrize("policy", [SINGLE_READ, TWO_READ], ids=["single_read", "two_read"])
 def test_fused_head_matches_generic(policy):
     nat, L = _lib()
     from model.mhc_common import MHCHead
@@ -183,6 +189,17 @@ def test_fused_head_matches_generic(policy):
     L.mhc_set_path_policy(GENERIC)
     y_g = head(x)
     L.mhc_set_path_policy(prev)
-    assert path == expected_path(n, c, policy, "head")
+    assert path == expected_path(n, c, policy, "head", t)
     assert L.mhc_device_error(1) == 0
     assert (y_g.float() - y_f.float()).abs().max().item() <= 2 ** -7 * y_g.float().abs().max().item()
+
+
+@pytest.mark.parametrize("n,c,t,with_res", [(4, 768, 4096, True), (4, 768, 32768, True), (4, 768, 2048, False),
+                                            (4, 1024, 2048, False), (8, 512, 260, False), (4, 256, 300, True)])
+def test_auto_policy_picks_the_measured_kernel(n, c, t, with_res):
+    """AUTO runs the kernel the C-ABI's measured rule names for the shape."""
+    gen = torch.Generator().manual_seed(t)
+    ps, _ = _params(n, c, with_res, gen)
+    xd = torch.randn(t, n * c, generator=gen).bfloat16().to(DEV)
+    _, path = _run_pre(xd, ps, with_res, n, c, AUTO)
+    assert path == expected_path(n, c, AUTO, "full" if with_res else "nohres", t)

@@ -83,10 +83,10 @@ def test_decoder_bf16_on_fused_kernels_matches_reference(case):
     assert paths[0] >= 1 and paths[1] == 1, "the sm_100a forward / tensor-core backward did not run"
     assert max_rel(g["logits"], logits) < 5e-2
     assert abs(float(loss) - float(g["loss"])) < 1e-2 * float(g["loss"])
-    # bf16 noise floor: gradients that are ~0 in the reference (layer 0's
-    # H_pre gates see n identical streams) come out as bf16 noise, so the bar
-    # is 25% of the gradient's own scale or 1e-3 of the largest mHC gradient
-    floor = 1e-3 * max(a.abs().max().item() for a in g["grads"])
+    # bf16 noise floor: gradients that are ~0 in the reference (the H_pre
+    # gates of layer 0 see n identical streams) come out as bf16 noise, so the
+    # bar is 25% of the gradient's own scale or 1% of the largest mHC gradient
+    floor = 1e-2 * max(a.abs().max().item() for a in g["grads"])
     for name, a, b in zip(g["grad_names"], g["grads"], grads):
         err = (a.float() - b.float().cpu()).abs().max().item()
         assert err < max(0.25 * a.abs().max().item(), floor), (name, err)
