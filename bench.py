@@ -84,7 +84,7 @@ def _bwd_bytes(n, c, sx, sf):
     return sx * (6 * n * c + c) + sf * 2 * c
 
 
-def _profiled_traffic(kernel, n, c, t, with_res):
+def _profiled_traffic(kernel, n, c, t, with_res, pre_path=1):
     """DRAM bytes (read + write) per launch of the dominant kernel from the
     committed ncu summary of this exact workload (profiles/*.md carries a line
     `traffic_bytes_per_launch: <int>` and the commit the capture was made at);
@@ -92,7 +92,8 @@ def _profiled_traffic(kernel, n, c, t, with_res):
     run."""
     if (n, c, t, bool(with_res)) != (4, 768, 32768, True):
         return None
-    name = {"pre": "pre_sr_kernel_config2.md", "post": "post_fwd_kernel_config2.md"}[kernel]
+    pre_name = "pre_sr_kernel_config2.md" if pre_path == 2 else "pre_tc_kernel_config2.md"
+    name = {"pre": pre_name, "post": "post_fwd_kernel_config2.md"}[kernel]
     path = os.path.join(ROOT, "profiles", name)
     out = {}
     try:
@@ -540,7 +541,7 @@ def run_ours(args, rank, world, local_rank):
     d_ms, d_bytes = calls[dom]
     achieved = d_bytes / (d_ms / 1e3) / 1e9
     layer_gbs = bytes_tok * t / (step_ms / 1e3) / 1e9  # per GPU, whole step
-    traffic = _profiled_traffic(dom, n, c, t, with_res)
+    traffic = _profiled_traffic(dom, n, c, t, with_res, fused_path)
 
     cpu = None
     if not args.no_cpu_baseline:
