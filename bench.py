@@ -700,21 +700,27 @@ def _train_step_entry(args, rank, world, dev):
     params = list(model.parameters())
     opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
     stream = torch.cuda.current_stream(dev)
+    buckets = GradBuckets(params, world) if world > 1 else None
     ar = []
 
     def step(timed):
         logits = model(ids)
         loss = F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), labels.view(-1)) + model.aux_loss()
         loss.backward()
-        if world > 1:
+        if buckets is not None:
+            # the buckets were all-reduced during backward as they completed;
+            # what remains on the stream after backward is the exposed part
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            allreduce_grads(params, world)
+            buckets.finish()
             e1.record(stream)
             if timed:
                 ar.append((e0, e1))
         opt.step()
-        opt.zero_grad(set_to_none=True)
+        if buckets is not None:
+            buckets.zero()
+        else:
+            opt.zero_grad(set_to_none=True)
 
     for _ in range(3):
         step(False)
@@ -734,8 +740,10 @@ def _train_step_entry(args, rank, world, dev):
     del model, opt
     torch.cuda.empty_cache()
     return {"tokens_per_s": world * batch * seq / (ms / 1e3), "ms_per_step": ms, "tokens_per_gpu": batch * seq,
-            "global_batch": f"{world * batch} x {seq}", "allreduce_ms_per_step": ar_ms,
-            "allreduce_share": ar_ms / ms if ms else 0.0,
+            "global_batch": f"{world * batch} x {seq}", "allreduce_exposed_ms_per_step": ar_ms,
+            "allreduce_exposed_share": ar_ms / ms if ms else 0.0,
+            "allreduce": "bucketed (32 MB), launched from gradient hooks during backward, fixed bucket order; "
+                         "exposed = the time from the end of backward to the last bucket's completion",
             "model": "MiniMind MoE (8 experts, top-2) + mHC on every sublayer: hidden 768, 8 layers, vocab 6400, "
                      "n=4, 20 Sinkhorn iterations; fwd + bwd + gradient all-reduce + AdamW"}
 
@@ -937,6 +945,77 @@ def allreduce_grads(params, world):
             off += p.numel()
 
 
+class GradBuckets:
+    """Gradient all-reduce overlapped with backward (what DDP does with
+    gradient_as_bucket_view): each parameter's .grad is a view into a
+    persistent flat buffer per dtype, cut into buckets of about `bucket_mb` in
+    reverse creation order (backward produces gradients roughly in that
+    order).  A post-accumulate hook counts a bucket's gradients; a bucket is
+    launched as an asynchronous all_reduce once it is complete and every
+    earlier bucket has been launched, so all ranks issue the same collectives
+    in the same order.  finish() launches what backward left incomplete (a
+    parameter that got no gradient on this rank, such as an expert no local
+    token was routed to, contributes its zeroed view), waits, and averages.
+    zero() clears the buffers in place; the views stay attached."""
+
+    def __init__(self, params, world, bucket_mb=32):
+        import torch.distributed as dist
+        self.dist, self.world = dist, world
+        self.params = [p for p in params if p.requires_grad]
+        self.flat = {}
+        self.buckets = []      # [dtype, start, end, [param ids], seen]
+        self.owner = {}
+        by_dtype = {}
+        for p in reversed(self.params):
+            by_dtype.setdefault(p.dtype, []).append(p)
+        cap = int(bucket_mb * (1 << 20))
+        for dt, ps in by_dtype.items():
+            total = sum(p.numel() for p in ps)
+            buf = torch.zeros(total, dtype=dt, device=ps[0].device)
+            self.flat[dt] = buf
+            off, cur = 0, None
+            for p in ps:
+                n = p.numel()
+                if cur is None or (cur[2] - cur[1]) * buf.element_size() >= cap:
+                    cur = [dt, off, off, [], 0]
+                    self.buckets.append(cur)
+                p.grad = buf[off:off + n].view_as(p)
+                cur[2] = off + n
+                cur[3].append(id(p))
+                self.owner[id(p)] = cur
+                off += n
+        self.index = {id(b): i for i, b in enumerate(self.buckets)}
+        self.handles = []
+        self.next = 0
+        self.hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in self.params]
+
+    def _ready(self, p):
+        b = self.owner[id(p)]
+        b[4] += 1
+        while self.next < len(self.buckets) and self.buckets[self.next][4] == len(self.buckets[self.next][3]):
+            self._launch(self.buckets[self.next])
+
+    def _launch(self, b):
+        dt, a, e = b[0], b[1], b[2]
+        self.handles.append((self.dist.all_reduce(self.flat[dt][a:e], async_op=True), b))
+        self.next += 1
+
+    def finish(self):
+        while self.next < len(self.buckets):
+            self._launch(self.buckets[self.next])
+        for h, b in self.handles:
+            h.wait()
+            self.flat[b[0]][b[1]:b[2]].div_(self.world)
+        self.handles = []
+        self.next = 0
+        for b in self.buckets:
+            b[4] = 0
+
+    def zero(self):
+        for buf in self.flat.values():
+            buf.zero_()
+
+
 def run_model(args, rank, world, local_rank):
     """configs[3] (--workload c4): forward of the 8-layer decoder, 32 x 2048
     tokens per GPU.  configs[4] (--workload c5): training step (forward,
@@ -961,6 +1040,7 @@ def run_model(args, rank, world, local_rank):
     dist = None
     if world > 1:
         import torch.distributed as dist
+    buckets = GradBuckets(params, world) if (train and world > 1 and not args.flat_allreduce) else None
 
     def step():
         if not train:
@@ -973,10 +1053,15 @@ def run_model(args, rank, world, local_rank):
         if aux is not None:
             loss = loss + aux  # the trainers' loss (trainer/train_pretrain.py:37)
         loss.backward()
-        if world > 1:
+        if buckets is not None:
+            buckets.finish()
+        elif world > 1:
             allreduce_grads(params, world)
         opt.step()
-        opt.zero_grad(set_to_none=True)
+        if buckets is not None:
+            buckets.zero()
+        else:
+            opt.zero_grad(set_to_none=True)
 
     for _ in range(args.warmup):
         step()
@@ -1039,6 +1124,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the token sweep, config-3 and fp32-stream sub-measurements")
     ap.add_argument("--no-train", action="store_true", help="skip the config-5 training-step sub-measurement")
+    ap.add_argument("--flat-allreduce", action="store_true",
+                    help="c5: one flat all-reduce per dtype after backward instead of the overlapped buckets")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

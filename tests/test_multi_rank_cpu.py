@@ -9,7 +9,10 @@ and check, with the oracle, that
   tokens, row for row;
 * all-reduced (summed) parameter gradients equal the full-batch gradients;
 * the timing reduction used by ``bench.py`` (max over ranks) picks the slowest
-  rank.
+  rank;
+* ``bench.py``'s gradient all-reduce handles a parameter with no gradient on
+  one rank, and its bucketed all-reduce (launched from gradient hooks during
+  backward) equals the flat one.
 """
 
 import os
@@ -158,3 +161,79 @@ def test_gradient_allreduce_with_a_missing_gradient():
         assert torch.allclose(torch.from_numpy(gs[0]), torch.full((5,), 1.5))
         assert torch.allclose(torch.from_numpy(gs[1]), torch.full((3, 2), 3.0))
         assert torch.allclose(torch.from_numpy(gs[2]), torch.full((4,), 3.0))  # (6 + 0) / 2
+
+
+def _bucket_worker(rank, port, q):
+    """bench.py's overlapped bucketed all-reduce against its flat all-reduce:
+    mixed fp32/bf16 parameters, many small buckets, an expert that gets no
+    gradient on rank 1, two steps (the views into the flat buffers must stay
+    attached across zero())."""
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+
+    def make():
+        torch.manual_seed(0)
+        m = torch.nn.ModuleDict({"a": torch.nn.Linear(8, 16), "b": torch.nn.Linear(16, 16),
+                                 "e0": torch.nn.Linear(16, 4, bias=False), "e1": torch.nn.Linear(16, 4, bias=False)})
+        m["b"].to(torch.bfloat16)
+        return m
+
+    def loss_of(m, x):
+        h = torch.tanh(m["a"](x))
+        h = m["b"](h.bfloat16()).float()
+        y = m["e0"](h)
+        if rank == 0:  # rank 1 routes nothing to expert 1
+            y = y + m["e1"](h)
+        return (y ** 2).mean()
+
+    try:
+        ref, buck = make(), make()
+        rp, bp = list(ref.parameters()), list(buck.parameters())
+        gb = bench.GradBuckets(bp, WORLD, bucket_mb=200 / (1 << 20))
+        assert len(gb.buckets) >= 4
+        out = []
+        for step in range(2):
+            gen = torch.Generator().manual_seed(10 * step + rank)
+            x = torch.randn(6, 8, generator=gen)
+            loss_of(ref, x).backward()
+            bench.allreduce_grads(rp, WORLD)
+            loss_of(buck, x).backward()
+            gb.finish()
+            out.append([(a.grad.float().clone(), b.grad.float().clone()) for a, b in zip(rp, bp)])
+            assert all(p.grad.data_ptr() >= gb.flat[p.dtype].data_ptr() for p in bp)
+            for p in rp:
+                p.grad = None
+            gb.zero()
+        t = torch.tensor([1.0])
+        dist.all_reduce(t)
+        q.put((rank, [[(a.numpy(), b.numpy()) for a, b in s] for s in out], t.item()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bucketed_allreduce_equals_flat_allreduce():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, port, q)) for r in range(WORLD)]
+    for pr in procs:
+        pr.start()
+    res = {}
+    for _ in range(WORLD):
+        r, steps, tsum = q.get(timeout=300)
+        res[r] = (steps, tsum)
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    for r in range(WORLD):
+        steps, tsum = res[r]
+        assert tsum == float(WORLD)
+        for pairs in steps:
+            for a, b in pairs:
+                assert torch.equal(torch.from_numpy(a), torch.from_numpy(b))
+    # both ranks hold the same averaged gradients
+    for (a0, _), (a1, _) in zip(res[0][0][1], res[1][0][1]):
+        assert torch.equal(torch.from_numpy(a0), torch.from_numpy(a1))
