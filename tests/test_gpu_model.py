@@ -6,9 +6,12 @@ inside the reference's block structure.
   by tests/golden/make_model_golden.py from the reference run on the CPU in
   fp32) load with ``strict=True``; its logits, next-token loss (plus the MoE
   auxiliary loss) and mHC parameter gradients must match the reference's.
-  fp32 runs take the generic kernels and must agree to 1e-4 relative; the bf16
-  run (mHC parameters fp32, as in the benchmark) takes the sm_100a kernels
-  (n*C = 512) and must agree within the bf16 tolerance.
+  fp32 runs take the generic kernels and must agree to 1e-4 relative.  The
+  bf16 run (mHC parameters fp32, as in the benchmark) takes the sm_100a
+  kernels (n*C = 512); it is checked against the same bf16 decoder on the
+  generic kernels (fp32 arithmetic, no tensor cores), which it must match
+  closely, and against the fp32 reference, which it may miss only by the bf16
+  model's own rounding noise: no more than the generic run misses it by.
 * A small bf16 decoder trains through the kernels with finite, non-zero mHC
   gradients.
 """
@@ -44,7 +47,17 @@ def _decoder_for(kw, dtype):
         iters=10, use_mhc=kw["use_mhc"], dtype=dtype)
 
 
-def _run(g, dtype):
+def _run(g, dtype, policy=None):
+    from model import _native as nat
+    prev = nat.lib().mhc_set_path_policy(policy) if policy is not None else None
+    try:
+        return _run_policy(g, dtype)
+    finally:
+        if prev is not None:
+            nat.lib().mhc_set_path_policy(prev)
+
+
+def _run_policy(g, dtype):
     from model import _native as nat
     m = _decoder_for(g["config"], dtype)
     sd = {k: v.float() for k, v in g["state_dict"].items()}
@@ -81,15 +94,26 @@ def test_decoder_bf16_on_fused_kernels_matches_reference(case):
     g = _golden()[case]
     logits, loss, _, grads, paths = _run(g, torch.bfloat16)
     assert paths[0] >= 1 and paths[1] == 1, "the sm_100a forward / tensor-core backward did not run"
+    _, loss_g, _, grads_g, paths_g = _run(g, torch.bfloat16, policy=1)
+    assert paths_g == (0, 0)
     assert max_rel(g["logits"], logits) < 5e-2
     assert abs(float(loss) - float(g["loss"])) < 1e-2 * float(g["loss"])
-    # bf16 noise floor: gradients that are ~0 in the reference (the H_pre
-    # gates of layer 0 see n identical streams) come out as bf16 noise, so the
-    # bar is 25% of the gradient's own scale or 1% of the largest mHC gradient
-    floor = 1e-2 * max(a.abs().max().item() for a in g["grads"])
-    for name, a, b in zip(g["grad_names"], g["grads"], grads):
-        err = (a.float() - b.float().cpu()).abs().max().item()
-        assert err < max(0.25 * a.abs().max().item(), floor), (name, err)
+    assert abs(float(loss) - float(loss_g)) < 1e-3 * float(loss_g)
+    big = max(a.abs().max().item() for a in g["grads"])
+    num = den = 0.0
+    for name, a, b, c in zip(g["grad_names"], g["grads"], grads, grads_g):
+        a, b, c = a.float(), b.float().cpu(), c.float().cpu()
+        # fused vs generic in the same bf16 model: only the projection's hi/lo
+        # split and the reduction order differ (measured <= 1e-3 * big)
+        assert (b - c).abs().max().item() < 2e-3 * big, name
+        # vs the fp32 reference: the bf16 model's own noise, which the
+        # generic run shows (gradients that are ~0 in the reference, such as
+        # the layer-0 H_pre gates that see n identical streams, are all noise)
+        err, err_g = (a - b).abs().max().item(), (a - c).abs().max().item()
+        assert err <= 1.5 * err_g + 1e-3 * big, (name, err, err_g)
+        num += ((a - b) ** 2).sum().item()
+        den += (a ** 2).sum().item()
+    assert (num / den) ** 0.5 < 0.1  # measured 0.007 (dense), 0.034 (MoE)
 
 
 @pytest.mark.parametrize("moe", [False, True], ids=["dense", "moe"])
