@@ -25,7 +25,10 @@ The same JSON line also carries, measured in the same run:
   * "fp32_stream": the layer with an fp32 residual stream and a bf16 sublayer
     output, the setting of the reference's bf16-autocast trainers;
   * "train_step": configs[4], the MoE + mHC training step (8 x 2048 tokens per
-    GPU), with the NCCL gradient all-reduce timed on its own.
+    GPU), with the NCCL gradient all-reduce timed on its own;
+  * "post_pre": the step between two sublayers (merge of one, coefficient
+    pass of the next, optionally its input RMSNorm) as two kernels and as the
+    fused merge + coefficient kernel.
 
 Multi-GPU: one process per GPU (torchrun), tokens sharded (weak scaling): every
 rank runs its own 16 x 2048 tokens with no collective on the data path.
@@ -410,6 +413,79 @@ def _layer_entry(lb, world, dev, steps, warmup, stream, peak, flush, with_bwd, s
     return e
 
 
+class PostPreBench:
+    """The step between two consecutive sublayers on a LayerBench's buffers:
+    the merge of this sublayer (x, f, H_res, H_post -> x') followed by the
+    coefficient pass of the next (same parameters) on x', either as the two
+    kernels (mhc_post_fwd, mhc_pre_fwd; plus torch's rms_norm on z for the
+    next sublayer's input norm) or as one mhc_post_pre_fwd call under
+    MHC_PATH_FUSED_POST_PRE (the fused merge + coefficient kernel, with the
+    norm in the same kernel)."""
+
+    def __init__(self, lb):
+        self.lb = lb
+        c = lb.c
+        self.x2 = torch.empty_like(lb.x)
+        self.z2 = torch.empty_like(lb.z)
+        self.y = torch.empty_like(lb.z)
+        self.hp2 = torch.empty_like(lb.h_post)
+        self.hr2 = torch.empty_like(lb.h_res) if lb.with_res else None
+        self.inv2 = torch.empty_like(lb.inv)
+        self.mix2 = torch.empty_like(lb.mix)
+        self.nw = torch.ones(c, device=lb.x.device)
+        self.nw_b = self.nw.to(lb.z.dtype)
+
+    def pair(self):
+        self.lb.post()
+        self.lb.pre(self.lb.out)
+
+    def pair_norm(self):
+        self.pair()
+        torch.nn.functional.rms_norm(self.lb.z, (self.lb.c,), self.nw_b, 1e-6)
+
+    def fused(self, norm=False):
+        lb, nat = self.lb, self.lb.nat
+        ps = lb.ps
+        prev = lb.L.mhc_set_path_policy(nat.PATH_FUSED_POST_PRE)
+        a_res, b_res = (ps[5], ps[6]) if lb.with_res else (None, None)
+        st = lb.L.mhc_post_pre_fwd(
+            nat.ptr(lb.x), lb.xc, nat.ptr(lb.h_res), nat.ptr(lb.h_post), nat.F32, nat.ptr(lb.f), lb.fc,
+            nat.ptr(self.x2), lb.t, lb.n, lb.c, nat.ptr(ps[0]), nat.ptr(ps[1]), nat.ptr(ps[2]), nat.ptr(ps[3]),
+            nat.ptr(ps[4]), nat.ptr(a_res), nat.ptr(b_res), nat.F32, int(lb.with_res), int(lb.with_res), lb.iters,
+            2.0, 1e-6, 1e-6, 1e-6, nat.ptr(self.z2), None, nat.ptr(self.hp2), nat.ptr(self.hr2), nat.F32,
+            nat.ptr(self.inv2), nat.ptr(self.mix2), nat.ptr(self.nw) if norm else None, nat.F32, 1e-6,
+            nat.ptr(self.y) if norm else None, nat.ptr(lb.ws), lb.ws.numel(), lb.sptr)
+        lb.L.mhc_set_path_policy(prev)
+        nat.check(st, "mhc_post_pre_fwd")
+
+    def fused_norm(self):
+        self.fused(True)
+
+
+def _post_pre_entry(lb, world, dev, steps, warmup, stream, peak):
+    """Two-kernel pair vs the fused merge + coefficient kernel, without and
+    with the next sublayer's input RMSNorm (whole job, median step)."""
+    pb = PostPreBench(lb)
+    n, c, t = lb.n, lb.c, lb.t
+    out = {"tokens_per_gpu": t, "n": n, "C": c, "with_res": lb.with_res}
+    pair_b = 2 * (3 * n * c + 2 * c)
+    fused_b = 2 * (2 * n * c + 2 * c)
+    for key, fns, nbytes in (("pair", [pb.pair], pair_b), ("pair_norm", [pb.pair_norm], pair_b + 2 * 2 * c),
+                             ("fused", [pb.fused], fused_b), ("fused_norm", [pb.fused_norm], fused_b + 2 * c)):
+        ms, _ = _time_steps(fns, steps, warmup, stream)
+        ms = _max_over_ranks(ms, world, dev)
+        gbs = nbytes * t / (ms / 1e3) / 1e9
+        out[key] = {"ms": ms, "tokens_per_s": world * t / (ms / 1e3), "algorithmic_bytes_per_token": nbytes,
+                    "gbs": gbs, "frac_of_measured": gbs / peak}
+        if key.startswith("fused"):
+            out[key]["path"] = lb.L.mhc_last_path()
+    out["speedup"] = out["pair"]["ms"] / out["fused"]["ms"]
+    out["speedup_with_norm"] = out["pair_norm"]["ms"] / out["fused_norm"]["ms"]
+    out["calls"] = ("pair: mhc_post_fwd + mhc_pre_fwd (+ torch rms_norm on z); fused: one mhc_post_pre_fwd "
+                    "(+ the norm in the same kernel)")
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -516,6 +592,10 @@ def run_ours(args, rank, world, local_rank):
             del lbs
             torch.cuda.empty_cache()
         extra["sweep"] = sweep
+        lbs = LayerBench(t, n, c, True, torch.bfloat16, torch.bfloat16, dev, stream, 66 + rank)
+        extra["post_pre"] = _post_pre_entry(lbs, world, dev, 20, 3, stream, peak)
+        del lbs
+        torch.cuda.empty_cache()
         for cc in (768, 1024):
             lbs = LayerBench(t, n, cc, False, torch.bfloat16, torch.bfloat16, dev, stream, 88 + rank)
             extra[f"nohres_c{cc}"] = _layer_entry(lbs, world, dev, 20, 3, stream, peak, flush, True, 2, 2)

@@ -94,6 +94,53 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C,
                 void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Forward: merge of sublayer l fused with the coefficient pass of l+1       */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of scratch `mhc_post_pre_fwd` needs (same as mhc_pre_fwd). */
+size_t mhc_post_pre_fwd_workspace(int64_t T, int n, int C, int with_res);
+
+/*
+ * One call for the step between two consecutive mHC sublayers, with the next
+ * sublayer's input RMSNorm:
+ *
+ *   x_out = x merged with sublayer l's output f:                         (f != NULL)
+ *           x_out[t, i*C+c] = sum_j h_res_prev[t,i,j] x[t, j*C+c] + h_post_prev[t,i] f[t,c]
+ *           (h_res_prev == NULL: H_res = I), exactly as mhc_post_fwd
+ *   z, h_pre, h_post, h_res, inv_rms, mixes = mhc_pre_fwd of sublayer l+1 on x_out
+ *           (on x itself when f == NULL; x_out, h_*_prev are then ignored)
+ *   y[t,c] = z[t,c] * rsqrt(mean_c z[t,:]^2 + norm_eps) * norm_weight[c]  (norm_weight != NULL)
+ *           the mean taken over z as stored (x_dtype); y has x_dtype
+ *
+ * Arguments after x_out have mhc_pre_fwd's meaning.  x_out must not alias x.
+ * For bf16 streams with n in {2, 4}, C a multiple of 128 with 4 <= C/128 <= 8
+ * and 16-byte aligned tensors, under MHC_PATH_FUSED_POST_PRE, the whole step
+ * is one sm_100a kernel (x read once, x_out and z written once: 2nC + 2C
+ * elements per token instead of the 3nC + 2C of mhc_post_fwd followed by
+ * mhc_pre_fwd; mhc_last_path() = 3); otherwise it runs mhc_post_fwd,
+ * mhc_pre_fwd and a row RMSNorm kernel, which is faster on B200 at every
+ * measured shape.
+ *
+ * Replaces the pair model/mhc_fused.py:828-832 (post phase of sublayer l) +
+ * :818-826 (pre phase of sublayer l+1) at the call sites
+ * model/model_minimind.py:338-339 (attention then MLP) and :392-400
+ * (consecutive blocks), and the input norms model/model_minimind.py:313-314
+ * (attn_in_norm / ffn_in_norm applied to z in the closures at :330, :336).
+ */
+int mhc_post_pre_fwd(const void *x, int x_dtype, const void *h_res_prev, const void *h_post_prev,
+                     int prev_coef_dtype, const void *f, int f_dtype, void *x_out,
+                     int64_t T, int n, int C,
+                     const void *phi, const void *alpha_pre, const void *bias_pre,
+                     const void *alpha_post, const void *bias_post,
+                     const void *alpha_res, const void *bias_res, int param_dtype,
+                     int with_res, int apply_sinkhorn, int sinkhorn_iters,
+                     float post_mult, float pre_eps, float rms_eps, float sinkhorn_eps,
+                     void *z, void *h_pre, void *h_post, void *h_res, int coef_dtype,
+                     float *inv_rms, float *mixes,
+                     const void *norm_weight, int norm_dtype, float norm_eps, void *y,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Forward: post / res merge                                                 */
 /* ------------------------------------------------------------------------ */
 
@@ -263,11 +310,16 @@ int mhc_device_sm_count(void);
 #define MHC_PATH_GENERIC     1
 #define MHC_PATH_TWO_READ    2
 #define MHC_PATH_SINGLE_READ 3
+/* As AUTO, and mhc_post_pre_fwd runs its fused merge + coefficient sm_100a
+ * kernel where it applies (under every other policy it runs the merge kernel,
+ * mhc_pre_fwd and a row RMSNorm kernel, measured faster on B200). */
+#define MHC_PATH_FUSED_POST_PRE 4
 int mhc_set_path_policy(int policy);
 
-/* Kernel the process's last mhc_pre_fwd / mhc_head_fwd ran (on any thread:
- * autograd runs backward on a thread of its own): 2 the single-read sm_100a
- * kernel, 1 the two-read sm_100a kernel, 0 the generic kernels; after
+/* Kernel the process's last mhc_pre_fwd / mhc_head_fwd / mhc_post_pre_fwd ran
+ * (on any thread: autograd runs backward on a thread of its own): 3 the fused
+ * merge + coefficient sm_100a kernel, 2 the single-read sm_100a kernel, 1 the
+ * two-read sm_100a kernel, 0 the generic kernels; after
  * mhc_pre_bwd / mhc_head_bwd: 1 if the tensor-core dx / dphi kernel ran, 0
  * for the generic kernels. */
 int mhc_last_path(void);
@@ -277,7 +329,9 @@ int mhc_last_path(void);
  * 1..6 = a bounded wait of the producer / MMA / row / coefficient /
  * pre-aggregate / Sinkhorn role of the two-read forward kernel ran out,
  * 21..26 = the producer / MMA / ingest / coefficient / Sinkhorn / z role of
- * the single-read forward kernel, 11..14 = one of the producer / MMA /
+ * the single-read forward kernel, 31..37 = the producer / MMA / row /
+ * coefficient / pre-aggregate / Sinkhorn / merge role of the fused merge +
+ * coefficient kernel, 11..14 = one of the producer / MMA /
  * epilogue / prep roles of the backward tensor-core kernel, 99 = the
  * self-test below).  A kernel whose wait runs out gives up
  * instead of hanging and overwrites the outputs it owns with NaN.

@@ -72,7 +72,8 @@ int *host_error_flag() { return g_host_flag.load(std::memory_order_acquire); }
 // no-H_res and head layers; the two-read kernel for long full-layer batches.
 static bool use_single_read(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C) {
   if (g_policy == MHC_PATH_SINGLE_READ) return pre_sr_eligible(mode, n, x_dtype, x, z, T, C);
-  if (g_policy != MHC_PATH_AUTO || !pre_sr_eligible(mode, n, x_dtype, x, z, T, C)) return false;
+  const bool automatic = g_policy == MHC_PATH_AUTO || g_policy == MHC_PATH_FUSED_POST_PRE;
+  if (!automatic || !pre_sr_eligible(mode, n, x_dtype, x, z, T, C)) return false;
   if (!pre_tc_eligible(mode, n, x_dtype, x, z, T, C)) return true;
   return mode != 0 || T < 32768;
 }
@@ -103,7 +104,7 @@ int mhc_device_sm_count(void) { return device_sm_count(); }
 int mhc_set_path_policy(int policy) {
   const int prev = g_policy;
   if (policy == MHC_PATH_AUTO || policy == MHC_PATH_GENERIC || policy == MHC_PATH_TWO_READ ||
-      policy == MHC_PATH_SINGLE_READ)
+      policy == MHC_PATH_SINGLE_READ || policy == MHC_PATH_FUSED_POST_PRE)
     g_policy = policy;
   return prev;
 }
@@ -112,8 +113,8 @@ int mhc_last_path(void) { return g_last_path.load(); }
 
 int mhc_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  const int words[4] = {read_sr_error(clear != 0), read_tc_error(clear != 0), read_tcb_error(clear != 0),
-                        read_selftest_error(clear != 0)};
+  const int words[5] = {read_sr_error(clear != 0), read_tc_error(clear != 0), read_tcb_error(clear != 0),
+                        read_ch_error(clear != 0), read_selftest_error(clear != 0)};
   for (int w : words)
     if (w < 0) return -1;
   for (int w : words)
@@ -204,6 +205,84 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
                                       device_sm_count(), s),
                       "mhc_pre_fwd coef"));
   return cuda_status(launch_aggregate(n, x_dtype, x, gate, z, T, C, s), "mhc_pre_fwd aggregate");
+}
+
+size_t mhc_post_pre_fwd_workspace(int64_t T, int n, int C, int with_res) {
+  return mhc_pre_fwd_workspace(T, n, C, with_res);
+}
+
+int mhc_post_pre_fwd(const void *x, int x_dtype, const void *h_res_prev, const void *h_post_prev,
+                     int prev_coef_dtype, const void *f, int f_dtype, void *x_out, int64_t T, int n, int C,
+                     const void *phi, const void *alpha_pre, const void *bias_pre, const void *alpha_post,
+                     const void *bias_post, const void *alpha_res, const void *bias_res, int param_dtype,
+                     int with_res, int apply_sinkhorn, int sinkhorn_iters, float post_mult, float pre_eps,
+                     float rms_eps, float sinkhorn_eps, void *z, void *h_pre, void *h_post, void *h_res,
+                     int coef_dtype, float *inv_rms, float *mixes, const void *norm_weight, int norm_dtype,
+                     float norm_eps, void *y, void *workspace, size_t workspace_bytes, void *stream) {
+  g_err[0] = 0;
+  MHC_TRY(check_shape(T, n, C));
+  const bool merge = f != nullptr, norm = norm_weight != nullptr;
+  if (!dtype_ok(x_dtype) || !dtype_ok(param_dtype) || !dtype_ok(coef_dtype) ||
+      (merge && (!dtype_ok(f_dtype) || !dtype_ok(prev_coef_dtype))) || (norm && !dtype_ok(norm_dtype)))
+    return fail(MHC_ERR_DTYPE, "mhc_post_pre_fwd: bad dtype code");
+  if (with_res != 0 && with_res != 1) return fail(MHC_ERR_SHAPE, "with_res must be 0 or 1");
+  if (sinkhorn_iters < 0 || sinkhorn_iters > 100000) return fail(MHC_ERR_SHAPE, "bad sinkhorn_iters %d", sinkhorn_iters);
+  if (!(norm_eps >= 0.f)) return fail(MHC_ERR_SHAPE, "mhc_post_pre_fwd: norm_eps must be >= 0");
+  if (T == 0) return MHC_OK;
+  if (!x || !phi || !alpha_pre || !bias_pre || !alpha_post || !bias_post || !z || !inv_rms || !mixes)
+    return fail(MHC_ERR_NULL, "mhc_post_pre_fwd: required pointer is NULL");
+  if (with_res && (!alpha_res || !bias_res)) return fail(MHC_ERR_NULL, "mhc_post_pre_fwd: alpha_res/bias_res NULL");
+  if (merge && (!h_post_prev || !x_out)) return fail(MHC_ERR_NULL, "mhc_post_pre_fwd: h_post_prev/x_out NULL");
+  if (merge && x_out == x) return fail(MHC_ERR_SHAPE, "mhc_post_pre_fwd: x_out must not alias x");
+  if (norm && !y) return fail(MHC_ERR_NULL, "mhc_post_pre_fwd: y NULL with norm_weight");
+  const size_t need = mhc_pre_fwd_workspace(T, n, C, with_res);
+  if (!workspace || workspace_bytes < need)
+    return fail(MHC_ERR_WORKSPACE, "mhc_post_pre_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (!aligned(workspace, 16) || !aligned(inv_rms, 4) || !aligned(mixes, 4))
+    return fail(MHC_ERR_ALIGN, "mhc_post_pre_fwd: workspace/inv_rms/mixes misaligned");
+  MHC_TRY(check_elem_align(x, x_dtype, "x"));
+  MHC_TRY(check_elem_align(z, x_dtype, "z"));
+  if (merge) {
+    MHC_TRY(check_elem_align(x_out, x_dtype, "x_out"));
+    MHC_TRY(check_elem_align(f, f_dtype, "f"));
+  }
+  if (norm) MHC_TRY(check_elem_align(y, x_dtype, "y"));
+  CoefParams p{alpha_pre, bias_pre, alpha_post, bias_post, alpha_res, bias_res, param_dtype,
+               post_mult, pre_eps, rms_eps, sinkhorn_eps, apply_sinkhorn ? 1 : 0, sinkhorn_iters};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int mode = with_res ? 0 : 1;
+  // The fused kernel only under MHC_PATH_FUSED_POST_PRE: on B200 the merge
+  // kernel followed by the coefficient kernel is measured faster (config 2,
+  // 32768 tokens, n = 4, C = 768: 158 us for the two against 171 us fused;
+  // with the input RMSNorm 214 us against 214 us).
+  const bool fused = g_policy == MHC_PATH_FUSED_POST_PRE && (!merge || f_dtype == MHC_BF16) &&
+                     post_pre_eligible(mode, n, x_dtype, x, f, x_out, z, y, T, C);
+  if (fused) {
+    cudaError_t e = launch_post_pre(mode, n, x, f, h_res_prev, h_post_prev, prev_coef_dtype, merge ? x_out : nullptr,
+                                    T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr, coef_dtype, inv_rms,
+                                    mixes, norm_weight, norm_dtype, norm_eps, norm ? y : nullptr, s);
+    if (e == cudaSuccess) {
+      g_last_path = 3;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_post_pre_fwd fused");
+    cudaGetLastError();  // not supported on this device: the separate kernels below
+  }
+  const void *src = x;
+  if (merge) {
+    MHC_TRY(cuda_status(launch_post_fwd(n, x_dtype, x, h_res_prev, prev_coef_dtype, h_post_prev, prev_coef_dtype, f,
+                                        f_dtype, x_out, T, C, 0, 0, 0.f, nullptr, s),
+                        "mhc_post_pre_fwd merge"));
+    src = x_out;
+  }
+  MHC_TRY(mhc_pre_fwd(src, x_dtype, T, n, C, phi, alpha_pre, bias_pre, alpha_post, bias_post, alpha_res, bias_res,
+                      param_dtype, with_res, apply_sinkhorn, sinkhorn_iters, post_mult, pre_eps, rms_eps,
+                      sinkhorn_eps, z, h_pre, h_post, h_res, coef_dtype, inv_rms, mixes, workspace,
+                      workspace_bytes, stream));
+  if (norm)
+    return cuda_status(launch_rmsnorm_rows(x_dtype, z, norm_weight, norm_dtype, norm_eps, y, T, C, s),
+                       "mhc_post_pre_fwd norm");
+  return MHC_OK;
 }
 
 int mhc_post_fwd(const void *x, int x_dtype, const void *h_res, int h_res_dtype, const void *h_post,

@@ -55,6 +55,20 @@ cudaError_t launch_pre_sr(int mode, int n, const void *x, int64_t T, int C, cons
                           int coef_dtype, float *inv_rms, float *mixes, cudaStream_t stream);
 int read_sr_error(bool clear);
 
+// ---- merge of sublayer l fused with the coefficient pass of l+1 (bf16) ----
+// n in {2, 4}, full or no-H_res, C a multiple of 128 with 4 <= C / 128 <= 8.
+// f == NULL: no merge (coefficient pass over x); norm_w == NULL: no RMSNorm.
+bool post_pre_eligible(int mode, int n, int x_dtype, const void *x, const void *f, const void *x_out,
+                       const void *z, const void *y, int64_t T, int C);
+cudaError_t launch_post_pre(int mode, int n, const void *x, const void *f, const void *h_res_prev,
+                            const void *h_post_prev, int prev_dtype, void *x_out, int64_t T, int C,
+                            const void *phi, const CoefParams &p, void *z, void *h_pre, void *h_post,
+                            void *h_res, int coef_dtype, float *inv_rms, float *mixes, const void *norm_w,
+                            int norm_dtype, float norm_eps, void *y, cudaStream_t stream);
+int read_ch_error(bool clear);
+cudaError_t launch_rmsnorm_rows(int z_dtype, const void *z, const void *w, int w_dtype, float eps, void *y,
+                                int64_t T, int C, cudaStream_t stream);
+
 cudaError_t launch_post_bwd(int n, int x_dtype, const void *dout, const void *x, const void *h_res,
                             int h_res_dtype, const void *h_post, int h_post_dtype, const void *f,
                             int f_dtype, void *dx, void *dh_res, void *dh_post, void *df,

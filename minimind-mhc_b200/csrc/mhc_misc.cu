@@ -1,5 +1,6 @@
 // Stand-alone Sinkhorn-Knopp (forward and backward-by-recompute, one thread per
-// matrix) and the StreamExpand copy / its reduction.
+// matrix), the StreamExpand copy / its reduction, and the row RMSNorm of the
+// generic post + pre path.
 #include "mhc_device.cuh"
 #include "mhc_dispatch.cuh"
 #include "mhc_kernels.h"
@@ -143,6 +144,34 @@ cudaError_t launch_expand_bwd(int dtype, const void *dout, void *dx, int64_t T, 
         (const Tx *)dout, (Tx *)dx, T, n, C);
     return cudaGetLastError();
   });
+}
+
+// y[t, c] = z[t, c] * rsqrt(mean_c z[t, :]^2 + eps) * w[c], one warp per row;
+// the mean is taken over the z values as stored.
+__global__ void __launch_bounds__(256)
+rmsnorm_rows_kernel(const void *__restrict__ z, int zdt, const void *__restrict__ w, int wdt, float eps,
+                    void *__restrict__ y, int64_t T, int C) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += nwarps) {
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float v = load_dyn(z, zdt, t * C + c);
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)C + eps);
+    for (int c = lane; c < C; c += 32)
+      store_dyn(y, zdt, t * C + c, load_dyn(z, zdt, t * C + c) * r * load_dyn(w, wdt, c));
+  }
+}
+
+cudaError_t launch_rmsnorm_rows(int z_dtype, const void *z, const void *w, int w_dtype, float eps, void *y,
+                                int64_t T, int C, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const unsigned grid = grid_for(T * 32, 256, device_sm_count(), 16);
+  rmsnorm_rows_kernel<<<grid, 256, 0, stream>>>(z, z_dtype, w, w_dtype, eps, y, T, C);
+  return cudaGetLastError();
 }
 
 }  // namespace mhc

@@ -268,6 +268,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for the 64-byte swizzle layout: rows of 64 B, 8-row groups 512 B
+// apart (SBO); the layout the TMA's 64-byte swizzle writes for a 32-column
+// bf16 box.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);       // start address
+  d |= (uint64_t)1 << 16;                              // leading byte offset (16 B)
+  d |= (uint64_t)(512 >> 4) << 32;                     // stride byte offset (512 B)
+  d |= (uint64_t)1 << 46;                              // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;                              // 64-byte swizzle
+  return d;
+}
+
 // UMMA shared-memory descriptor, general form: leading / stride byte offsets
 // and the layout type (0 = no swizzle, 2 = 128-byte swizzle).
 __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
@@ -417,6 +430,8 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// all but the newest committed group of this thread are complete
+__device__ __forceinline__ void bulk_wait_all_but_one() { asm volatile("cp.async.bulk.wait_group 1;" ::: "memory"); }
 // every committed store of this thread has finished reading shared memory
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // every committed store of this thread is complete

@@ -35,6 +35,10 @@ _PROTOS = {
     "mhc_pre_fwd_workspace": (_SZ, [_I64, _I, _I, _I]),
     "mhc_pre_fwd": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
                          _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P, _SZ, _P]),
+    "mhc_post_pre_fwd_workspace": (_SZ, [_I64, _I, _I, _I]),
+    "mhc_post_pre_fwd": (_I, [_P, _I, _P, _P, _I, _P, _I, _P, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I,
+                              _I, _I, _I, _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P, _I, _F, _P, _P,
+                              _SZ, _P]),
     "mhc_post_fwd": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _I64, _I, _I, _I, _I, _F, _P, _P]),
     "mhc_post_bwd": (_I, [_P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _I64, _I, _I, _P]),
     "mhc_pre_bwd_workspace": (_SZ, [_I64, _I, _I, _I, _I, _I]),
@@ -59,7 +63,9 @@ _PROTOS = {
                                  _F, _F, _F, _F, _P, _P, _P, _P, _I, _P, _P, _P]),
 }
 
-PATH_AUTO, PATH_GENERIC, PATH_TWO_READ, PATH_SINGLE_READ = 0, 1, 2, 3
+PATH_AUTO, PATH_GENERIC, PATH_TWO_READ, PATH_SINGLE_READ, PATH_FUSED_POST_PRE = 0, 1, 2, 3, 4
+# mhc_last_path() after a forward call: the kernel family that ran
+RAN_GENERIC, RAN_TWO_READ, RAN_SINGLE_READ, RAN_POST_PRE = 0, 1, 2, 3
 
 EXPORTED = tuple(_PROTOS)
 
@@ -143,7 +149,11 @@ ERROR_ROLES = {1: "forward TMA producer", 2: "forward MMA issuer", 3: "forward r
                14: "backward prep warps", 21: "single-read forward TMA producer",
                22: "single-read forward MMA issuer", 23: "single-read forward ingest warps",
                24: "single-read forward coefficient warp", 25: "single-read forward Sinkhorn warps",
-               26: "single-read forward z warps", 99: "bounded-wait self-test"}
+               26: "single-read forward z warps", 31: "merge + coefficient TMA producer",
+               32: "merge + coefficient MMA issuer", 33: "merge + coefficient row warps",
+               34: "merge + coefficient coefficient warp", 35: "merge + coefficient pre-aggregate warps",
+               36: "merge + coefficient Sinkhorn warp", 37: "merge + coefficient merge warps",
+               99: "bounded-wait self-test"}
 
 _flag_tensor = None   # pinned int32 host tensor registered with the library
 _flag_word = None     # ctypes view of its first element
