@@ -486,6 +486,30 @@ def _post_pre_entry(lb, world, dev, steps, warmup, stream, peak):
     return out
 
 
+def run_post_pre(args, rank, world, local_rank):
+    """--workload post_pre: config 2's step between two sublayers (merge of one,
+    coefficient pass and input RMSNorm of the next), as the two-kernel pair and
+    as the fused merge + coefficient kernel, K steps each after W warm-ups."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = _peaks()
+    lb = LayerBench(args.tokens, 4, 768, args.variant == "full", torch.bfloat16, torch.bfloat16, dev, stream,
+                    66 + rank)
+    e = _post_pre_entry(lb, world, dev, args.steps, args.warmup, stream, peak)
+    if rank != 0:
+        return
+    ms = e["fused"]["ms"]
+    print(json.dumps({"metric": "mHC post+pre step tokens/s", "value": e["fused"]["tokens_per_s"],
+                      "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": f"post_pre: merge of sublayer l + coefficient pass of l+1, "
+                                             f"{args.tokens} tokens/GPU, C=768, n=4, {args.variant}",
+                                 "l2": "inputs larger than L2" if args.tokens >= 16384 else "inputs fit in L2"},
+                      "peak_kind": peak_kind, "post_pre": e}))
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -1191,8 +1215,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["layer", "c4", "c5"], default="layer",
-                    help="layer: configs[1] mHC layer (the headline); c4 / c5: model-level configs[3] / [4]")
+    ap.add_argument("--workload", choices=["layer", "c4", "c5", "post_pre"], default="layer",
+                    help="layer: configs[1] mHC layer (the headline); c4 / c5: model-level configs[3] / [4]; "
+                         "post_pre: the step between two sublayers, two kernels against the fused kernel")
     ap.add_argument("--variant", choices=["full", "nohres"], default="full")
     ap.add_argument("--C", type=int, default=0, help="stream width for --variant nohres (768 or 1024)")
     ap.add_argument("--tokens", type=int, default=16 * 2048)
@@ -1228,6 +1253,8 @@ def main():
     try:
         if args.workload == "layer":
             run_ours(args, rank, world, local_rank)
+        elif args.workload == "post_pre":
+            run_post_pre(args, rank, world, local_rank)
         else:
             run_model(args, rank, world, local_rank)
     finally:

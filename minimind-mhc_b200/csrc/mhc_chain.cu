@@ -66,6 +66,9 @@ namespace ch {
 
 using namespace sm100;
 
+#ifndef MHC_CH_STORE_HINT
+#define MHC_CH_STORE_HINT 1
+#endif
 constexpr int TM = 128;              // tokens per tile (UMMA M)
 constexpr int COLS = 128;            // columns of every stream owned by a CTA
 constexpr int QC = 32;               // columns per chunk (a quarter of the CTA's 128)
@@ -437,9 +440,14 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
             // which the merge has read) are free once the stores have read them
             const uint32_t q0 = q - NL;
 #pragma unroll
-            for (int i = 0; i < N; ++i)
+            for (int i = 0; i < N; ++i) {
+#if MHC_CH_STORE_HINT
               tma_store_2d_hint(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * CHUNK, i * a.C + c0 + qq * QC,
                                 tile * TM, opol);
+#else
+              tma_store_2d(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * CHUNK, i * a.C + c0 + qq * QC, tile * TM);
+#endif
+            }
             bulk_commit();
             mbar_arrive(BAR(B_EMPTY + (q0 + N) % RING));
             mbar_arrive(BAR(B_EMPTY + (q0 + N) % RING));
