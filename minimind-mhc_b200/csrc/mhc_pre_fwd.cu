@@ -31,6 +31,7 @@ struct CoefCfg {
   static constexpr int FDP = JG * RJ;
   static constexpr int SEGS = TM * 8;                            // 16 B segments per chunk
   static constexpr int SEG_IT = (SEGS + THREADS - 1) / THREADS;
+  static constexpr int PH_IT = (KC * FD + THREADS - 1) / THREADS;  // phi elements per thread per chunk
   static constexpr int MRS = FD + 1;
   static constexpr int NPAR = 3 + 2 * N + N * N;
   static constexpr size_t SMEM_X = size_t(TM) * XS * 4;
@@ -80,7 +81,9 @@ coef_fwd_kernel(const Tx *__restrict__ x, int64_t T, int nC, const void *__restr
   for (int i = tid; i < (Cf::FDP - FD) * XS; i += Cf::THREADS) ps[FD * XS + i] = 0.f;
 
   const int nchunks = (nC + KC - 1) / KC;
-  uint4 pre[Cf::SEG_IT];  // raw Tx elements of the next chunk
+  uint4 pre[Cf::SEG_IT];     // raw Tx elements of the next chunk
+  float phv[Cf::PH_IT];      // phi elements of the next chunk (loaded a chunk ahead: the loads'
+                             // latency overlaps the FMA loop instead of stalling every chunk)
   float ssq_part[Cf::SEG_IT];
 #pragma unroll
   for (int s = 0; s < Cf::SEG_IT; ++s) ssq_part[s] = 0.f;
@@ -102,6 +105,13 @@ coef_fwd_kernel(const Tx *__restrict__ x, int64_t T, int nC, const void *__restr
         for (int e = 0; e < VEC; ++e)
           if (seg < Cf::SEGS && tok < T && k + e < nC) e8[e] = x[tok * nC + k + e];
       }
+    }
+    const int dt = p.param_dtype;
+#pragma unroll
+    for (int u = 0; u < Cf::PH_IT; ++u) {
+      const int e = tid + u * Cf::THREADS;
+      const int kk = e / FD, j = e - kk * FD;
+      phv[u] = (e < KC * FD && k0 + kk < nC) ? load_dyn(phi, dt, (int64_t)(k0 + kk) * FD + j) : 0.f;
     }
   };
 
@@ -133,15 +143,13 @@ coef_fwd_kernel(const Tx *__restrict__ x, int64_t T, int nC, const void *__restr
         }
       }
     }
-    // stage phi^T chunk (fp32)
-    {
-      const int k0 = kc * KC;
-      const int dt = p.param_dtype;
-      for (int e = tid; e < KC * FD; e += Cf::THREADS) {
+    // stage phi^T chunk (fp32), loaded with the chunk's x
+#pragma unroll
+    for (int u = 0; u < Cf::PH_IT; ++u) {
+      const int e = tid + u * Cf::THREADS;
+      if (e < KC * FD) {
         const int kk = e / FD, j = e - kk * FD;
-        float v = 0.f;
-        if (k0 + kk < nC) v = load_dyn(phi, dt, (int64_t)(k0 + kk) * FD + j);
-        ps[j * XS + kk] = v;
+        ps[j * XS + kk] = phv[u];
       }
     }
     __syncthreads();

@@ -58,7 +58,10 @@ namespace tc {
 
 using namespace sm100;
 
-constexpr int S = 8;                 // CTAs per cluster (K split)
+#ifndef MHC_TC_S
+#define MHC_TC_S 8
+#endif
+constexpr int S = MHC_TC_S;          // CTAs per cluster (K split); above 8 a non-portable cluster size
 constexpr int TM = 128;              // tokens per tile (UMMA M)
 constexpr int RING_MAX = 12;         // x chunk slots (runtime count <= this)
 // tokens per pre-aggregate box: 32 or 16 (a quarter or an eighth of a tile),
@@ -600,7 +603,7 @@ pre_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __nv_bfloat16 *__r
         }
         const int my_lt = lt + half, hb = my_lt % HBL;
         const int64_t tok = (int64_t)(tile + half * (int)ncl) * TM + (int)rank * TPC + (lane & 15);
-        if ((half == 0 || two) && tok < a.T) {
+        if ((half == 0 || two) && (lane & 15) < TPC && tok < a.T) {
           float hm[N * N];
 #pragma unroll
           for (int k = 0; k < N * N; ++k) hm[k] = lg[(hb * TPC + (lane & 15)) * 16 + k];
@@ -844,6 +847,10 @@ static cudaError_t launch_impl(const void *x, int64_t T, int C, Args args, cudaS
       if (g_kerns[i].kern == (const void *)kern && g_kerns[i].dev == dev) ke = &g_kerns[i];
     if (!ke) {
       if (g_kerns_n == 64) return cudaErrorNotSupported;
+      if (S > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+      }
       ke = &g_kerns[g_kerns_n++];
       *ke = KernEntry{(const void *)kern, dev, 0, 0, 0};
     }
