@@ -443,10 +443,10 @@ class PostPreBench:
         self.pair()
         torch.nn.functional.rms_norm(self.lb.z, (self.lb.c,), self.nw_b, 1e-6)
 
-    def fused(self, norm=False):
+    def fused(self, norm=False, policy=None):
         lb, nat = self.lb, self.lb.nat
         ps = lb.ps
-        prev = lb.L.mhc_set_path_policy(nat.PATH_FUSED_POST_PRE)
+        prev = lb.L.mhc_set_path_policy(nat.PATH_FUSED_POST_PRE if policy is None else policy)
         a_res, b_res = (ps[5], ps[6]) if lb.with_res else (None, None)
         st = lb.L.mhc_post_pre_fwd(
             nat.ptr(lb.x), lb.xc, nat.ptr(lb.h_res), nat.ptr(lb.h_post), nat.F32, nat.ptr(lb.f), lb.fc,
@@ -461,6 +461,16 @@ class PostPreBench:
     def fused_norm(self):
         self.fused(True)
 
+    def call(self):
+        """mhc_post_pre_fwd under the default policy (merge kernel, the fastest
+        coefficient kernel, no norm)."""
+        self.fused(False, self.lb.nat.PATH_AUTO)
+
+    def call_norm(self):
+        """mhc_post_pre_fwd under the default policy with the input norm (merge
+        kernel, the fastest coefficient kernel, the row RMSNorm kernel)."""
+        self.fused(True, self.lb.nat.PATH_AUTO)
+
 
 def _post_pre_entry(lb, world, dev, steps, warmup, stream, peak):
     """Two-kernel pair vs the fused merge + coefficient kernel, without and
@@ -471,18 +481,21 @@ def _post_pre_entry(lb, world, dev, steps, warmup, stream, peak):
     pair_b = 2 * (3 * n * c + 2 * c)
     fused_b = 2 * (2 * n * c + 2 * c)
     for key, fns, nbytes in (("pair", [pb.pair], pair_b), ("pair_norm", [pb.pair_norm], pair_b + 2 * 2 * c),
-                             ("fused", [pb.fused], fused_b), ("fused_norm", [pb.fused_norm], fused_b + 2 * c)):
+                             ("fused", [pb.fused], fused_b), ("fused_norm", [pb.fused_norm], fused_b + 2 * c),
+                             ("call", [pb.call], pair_b), ("call_norm", [pb.call_norm], pair_b + 2 * 2 * c)):
         ms, _ = _time_steps(fns, steps, warmup, stream)
         ms = _max_over_ranks(ms, world, dev)
         gbs = nbytes * t / (ms / 1e3) / 1e9
         out[key] = {"ms": ms, "tokens_per_s": world * t / (ms / 1e3), "algorithmic_bytes_per_token": nbytes,
                     "gbs": gbs, "frac_of_measured": gbs / peak}
-        if key.startswith("fused"):
+        if key.startswith("fused") or key.startswith("call"):
             out[key]["path"] = lb.L.mhc_last_path()
     out["speedup"] = out["pair"]["ms"] / out["fused"]["ms"]
     out["speedup_with_norm"] = out["pair_norm"]["ms"] / out["fused_norm"]["ms"]
+    out["call_norm_speedup"] = out["pair_norm"]["ms"] / out["call_norm"]["ms"]
     out["calls"] = ("pair: mhc_post_fwd + mhc_pre_fwd (+ torch rms_norm on z); fused: one mhc_post_pre_fwd "
-                    "(+ the norm in the same kernel)")
+                    "under MHC_PATH_FUSED_POST_PRE (+ the norm in the same kernel); call: one mhc_post_pre_fwd "
+                    "under the default policy (merge kernel, fastest coefficient kernel, row RMSNorm kernel)")
     return out
 
 

@@ -166,10 +166,90 @@ rmsnorm_rows_kernel(const void *__restrict__ z, int zdt, const void *__restrict_
   }
 }
 
+// The same with 16-byte vectors (16-bit z, C a multiple of 8, aligned rows):
+// a warp keeps VPL vectors of each of two rows in registers (one HBM read of
+// z) and reduces the two rows together, so their loads and shuffles overlap.
+template <typename Tz, typename Tw, int VPL>
+__global__ void __launch_bounds__(256)
+rmsnorm_rows_vec_kernel(const Tz *__restrict__ z, const Tw *__restrict__ w, float eps, Tz *__restrict__ y,
+                        int64_t T, int C) {
+  constexpr int VEC = 8;
+  extern __shared__ float ws[];  // the norm weight in fp32, staged once per block
+  for (int c = threadIdx.x; c < C; c += blockDim.x) ws[c] = to_f(w[c]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, nv = C / VEC;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2; t0 < T; t0 += nwarps * 2) {
+    Pack<Tz> pk[2][VPL];
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        const int v = lane + 32 * u;
+        pk[r][u].raw = (t0 + r < T && v < nv) ? ldg_stream(z + (t0 + r) * C + v * VEC) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int u = 0; u < VPL; ++u)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) ss[r] = fmaf(pk[r][u].get(e), pk[r][u].get(e), ss[r]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], o);
+      ss[1] += __shfl_xor_sync(0xffffffffu, ss[1], o);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (t0 + r >= T) continue;
+      const float rr = rsqrtf(ss[r] / (float)C + eps);
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        const int v = lane + 32 * u;
+        if (v >= nv) continue;
+        const float4 w0 = *reinterpret_cast<const float4 *>(ws + v * VEC);
+        const float4 w1 = *reinterpret_cast<const float4 *>(ws + v * VEC + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        Pack<Tz> o;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o.set(e, pk[r][u].get(e) * rr * wv[e]);
+        stg_stream(y + (t0 + r) * C + v * VEC, o.raw);
+      }
+    }
+  }
+}
+
 cudaError_t launch_rmsnorm_rows(int z_dtype, const void *z, const void *w, int w_dtype, float eps, void *y,
                                 int64_t T, int C, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const unsigned grid = grid_for(T * 32, 256, device_sm_count(), 16);
+  const size_t smem = (size_t)C * 4;
+  const bool vec = z_dtype != MHC_F32 && C % 8 == 0 && C <= 2048 && ((uintptr_t)z & 15) == 0 &&
+                   ((uintptr_t)y & 15) == 0;
+  if (vec) {
+    const int vpl = (C / 8 + 31) / 32;  // vectors of a row per lane
+    auto go = [&](auto vtag) -> cudaError_t {
+      constexpr int VPL = decltype(vtag)::value;
+      const unsigned g2 = grid_for((T + 1) / 2 * 32, 256, device_sm_count(), 16);
+      return with_dtype(w_dtype, [&](auto wtag) -> cudaError_t {
+        using Tw = decltype(wtag);
+        if (z_dtype == MHC_BF16)
+          rmsnorm_rows_vec_kernel<__nv_bfloat16, Tw, VPL><<<g2, 256, smem, stream>>>(
+              (const __nv_bfloat16 *)z, (const Tw *)w, eps, (__nv_bfloat16 *)y, T, C);
+        else
+          rmsnorm_rows_vec_kernel<__half, Tw, VPL><<<g2, 256, smem, stream>>>((const __half *)z, (const Tw *)w, eps,
+                                                                             (__half *)y, T, C);
+        return cudaGetLastError();
+      });
+    };
+    if (vpl <= 1) return go(IC<1>{});
+    if (vpl <= 2) return go(IC<2>{});
+    if (vpl <= 3) return go(IC<3>{});
+    if (vpl <= 4) return go(IC<4>{});
+    if (vpl <= 8) return go(IC<8>{});
+  }
   rmsnorm_rows_kernel<<<grid, 256, 0, stream>>>(z, z_dtype, w, w_dtype, eps, y, T, C);
   return cudaGetLastError();
 }
