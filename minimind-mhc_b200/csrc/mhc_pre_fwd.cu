@@ -20,10 +20,13 @@ struct CoefCfg {
   static constexpr int FD = Dims<N, MODE>::FD;
   static constexpr int JG = FD <= 32 ? 4 : (FD <= 96 ? 8 : 32);  // column groups per warp
   static constexpr int RJ = (FD + JG - 1) / JG;                  // columns per thread
-  static constexpr int RT = 2;                                   // tokens per thread
+  // tokens per thread and block size: fp32 x takes 4 tokens per thread in
+  // 128-thread blocks (twice the FMAs per shared-memory load: the fp32 kernel
+  // is bound by shared-memory wavefronts), 16-bit x 2 in 256-thread blocks
+  static constexpr int RT = sizeof(Tx) == 4 ? 4 : 2;
   static constexpr int TG = 32 / JG;                             // token groups per warp
   static constexpr int TPW = TG * RT;                            // tokens per warp
-  static constexpr int THREADS = 256;
+  static constexpr int THREADS = sizeof(Tx) == 4 ? 128 : 256;
   static constexpr int TM = (THREADS / 32) * TPW;                // tokens per block
   static constexpr int VEC = 16 / sizeof(Tx);
   static constexpr int KC = 8 * VEC;                             // 128 bytes of a row
