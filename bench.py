@@ -870,7 +870,7 @@ def _train_step_entry(args, rank, world, dev):
 # ---------------------------------------------------------------------------
 
 def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=4, inter=2048, vocab=6400,
-                   experts=8, topk=2, moe_inter=None, theta=1e6, eps=1e-6, iters=20, use_mhc=1,
+                   experts=8, topk=2, moe_inter=None, theta=1e6, eps=1e-6, iters=20, use_mhc=1, chain=False,
                    aux_coef=5e-4, dtype=torch.bfloat16):
     """The reference's model with this build's mHC modules: a module tree whose
     state_dict keys, shapes and forward math are those of the reference's
@@ -995,6 +995,7 @@ def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=
             self.embed_up_norm = nn.Sequential(nn.RMSNorm(hidden, eps=eps), StreamExpand(n, hidden))
             self.layers = nn.ModuleList([MiniMindBlock() for _ in range(layers)])
             self.norm = nn.Sequential(MHCHead(n, hidden, eps=eps), nn.RMSNorm(hidden, eps=eps))
+            self.use_chain = chain
 
         def forward(self, ids):
             l = ids.shape[1]
@@ -1004,8 +1005,19 @@ def _build_decoder(moe: bool, dev, n=4, hidden=768, layers=8, heads=8, kv_heads=
             cos = torch.cat([ang.cos(), ang.cos()], dim=-1)[None, :, None, :]
             sin = torch.cat([ang.sin(), ang.sin()], dim=-1)[None, :, None, :]
             h = self.embed_up_norm(self.embed_tokens(ids))
-            for blk in self.layers:
-                h = blk(h, cos, sin)
+            if self.use_chain:
+                # every sublayer through the block-level API: the merge of one
+                # sublayer, the coefficient pass and the input norm of the next
+                # in one mhc_post_pre_fwd call (model/mhc_block.py)
+                from model.mhc_block import mhc_chain
+                steps = []
+                for blk in self.layers:
+                    steps.append((blk.attn_mhc, lambda y, blk=blk: blk.self_attn(y, cos, sin), blk.attn_in_norm))
+                    steps.append((blk.mlp_mhc, blk.mlp, blk.ffn_in_norm))
+                h = mhc_chain(h, steps)
+            else:
+                for blk in self.layers:
+                    h = blk(h, cos, sin)
             return self.norm(h)
 
     class MiniMindForCausalLM(nn.Module):
@@ -1146,7 +1158,7 @@ def run_model(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     train = args.workload == "c5"
     torch.manual_seed(1234 + rank)
-    model = _build_decoder(moe=train, dev=dev)
+    model = _build_decoder(moe=train, dev=dev, chain=args.chain)
     batch = 8 if train else 32
     seq = 2048
     gen = torch.Generator(device=dev).manual_seed(77 + rank)
@@ -1216,6 +1228,8 @@ def run_model(args, rank, world, local_rank):
             "model": "hidden 768, 8 layers, 8 q / 4 kv heads, RoPE 1e6, SwiGLU 2048, vocab 6400, n=4, "
                      "20 Sinkhorn iterations",
             "global_batch": world * batch, "seq_len": seq, "parallelism": f"dp{world}",
+            "mhc_api": "block-level mhc_chain (merge + next coefficient pass + input norm per call)"
+                       if args.chain else "drop-in modules, input norms in the closures",
         },
         "clocks": clocks,
     }
@@ -1242,6 +1256,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the token sweep, config-3 and fp32-stream sub-measurements")
     ap.add_argument("--no-train", action="store_true", help="skip the config-5 training-step sub-measurement")
+    ap.add_argument("--chain", action="store_true",
+                    help="c4 / c5: run the decoder's sublayers through the block-level mhc_chain API")
     ap.add_argument("--flat-allreduce", action="store_true",
                     help="c5: one flat all-reduce per dtype after backward instead of the overlapped buckets")
     args = ap.parse_args()

@@ -70,7 +70,9 @@ RAN_GENERIC, RAN_TWO_READ, RAN_SINGLE_READ, RAN_POST_PRE = 0, 1, 2, 3
 EXPORTED = tuple(_PROTOS)
 
 _lib = None
-_lock = threading.Lock()
+# re-entrant: registering the error flag (under the lock) loads the library
+# (which takes the lock again) when the first native call is a call()
+_lock = threading.RLock()
 
 
 def load_library(path: str | None = None):

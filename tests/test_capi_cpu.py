@@ -99,3 +99,26 @@ def test_workspace_queries(lib):
     b = lib.mhc_pre_bwd_workspace(32768, 4, 768, 1, 1, 20)
     assert b >= 32768 * 24 * 4
     assert lib.mhc_pre_bwd_workspace(1, 3, 768, 1, 1, 20) == 0  # invalid n
+
+
+def test_first_native_call_loads_the_library_without_deadlock():
+    """A process whose first native call is model._native.call() (the library
+    not loaded yet) registers the error flag under the module lock, which loads
+    the library under the same lock: the lock must be re-entrant.  Run in a
+    fresh interpreter with pinning stubbed out (no GPU here); the flag
+    registration then fails with a RuntimeError instead of hanging."""
+    import subprocess
+    import sys as _sys
+    pkg = os.path.join(ROOT, "minimind-mhc_b200")
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import torch\n"
+        "torch.Tensor.pin_memory = lambda self: self\n"
+        "from model import _native as nat\n"
+        "try:\n"
+        "    nat.call('mhc_abi_version')\n"
+        "except RuntimeError:\n"
+        "    pass\n"
+        "print('returned')\n" % pkg)
+    r = subprocess.run([_sys.executable, "-c", code], capture_output=True, timeout=60)
+    assert b"returned" in r.stdout, r.stderr.decode(errors="replace")[-2000:]

@@ -138,3 +138,30 @@ def test_small_decoder_trains_through_mhc_kernels(moe):
         assert p.dtype == torch.float32, n
         assert p.grad is not None and torch.isfinite(p.grad).all(), n
     assert sum(float(p.grad.abs().sum()) for _, p in mhc) > 0
+
+
+@pytest.mark.parametrize("moe", [False, True], ids=["dense", "moe"])
+def test_decoder_on_the_chain_api_matches_the_modules(moe):
+    """The benchmark decoder with its sublayers run through mhc_chain (each
+    block's input norms handed to the chain) against the same decoder calling
+    the drop-in modules with the norms in the closures: same logits and
+    gradients up to bf16 rounding."""
+    import bench
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    m = bench._build_decoder(moe=moe, dev=dev, hidden=256, layers=2, heads=4, kv_heads=2, inter=512, vocab=512)
+    ids = torch.randint(0, 512, (2, 256), device=dev)
+    outs = []
+    for chain in (False, True):
+        m.model.use_chain = chain
+        m.zero_grad(set_to_none=True)
+        logits = m(ids)
+        loss = F.cross_entropy(logits.view(-1, 512).float(), ids.view(-1))
+        loss.backward()
+        outs.append((logits.detach().float(), {n: p.grad.detach().float().clone() for n, p in m.named_parameters()
+                                               if p.grad is not None}))
+    (l0, g0), (l1, g1) = outs
+    assert (l0 - l1).abs().max().item() <= 2e-2 * l0.abs().max().item()
+    assert set(g0) == set(g1)
+    for n in g0:
+        assert (g0[n] - g1[n]).abs().max().item() <= 5e-2 * g0[n].abs().max().item() + 1e-6, n
