@@ -22,7 +22,7 @@ sublayer 0, then L-1 calls of ``mhc_post_pre_fwd`` (the merge of sublayer l
 and the coefficient pass + norm of sublayer l+1 in one sm_100a kernel), then
 the merge of the last sublayer.  Backward runs the same kernels as the
 drop-in modules (coefficient backward by recompute, merge backward); the
-RMSNorm backward is a few PyTorch element-wise ops on z.
+RMSNorm backward recomputes torch's rms_norm on z under autograd.
 """
 
 from __future__ import annotations
@@ -97,19 +97,19 @@ def _post_pre_fwd(x2d, hr_prev, hp_prev, f2d, ps, meta, norm_w, norm_eps):
 
 
 def _norm_bwd(g_y, z, w, eps):
-    """Gradient of y = z * rsqrt(mean(z^2) + eps) * w w.r.t. z and w (fp32 math)."""
-    zf = z.float()
-    r = torch.rsqrt(zf.pow(2).mean(-1, keepdim=True) + eps)
-    yhat = zf * r
-    g = g_y.float()
-    dw = (g * yhat).sum(0)
-    gw = g * w.float()
-    dz = r * (gw - yhat * (gw * yhat).mean(-1, keepdim=True))
+    """Gradient of y = z * rsqrt(mean(z^2) + eps) * w w.r.t. z and w: torch's
+    rms_norm recomputed under autograd (its fused kernels when z and w share a
+    dtype), one forward and one backward pass over z."""
+    with torch.enable_grad():
+        zz = z.detach().requires_grad_(True)
+        ww = w.detach().requires_grad_(True)
+        yy = torch.nn.functional.rms_norm(zz, (z.shape[-1],), ww, eps)
+        dz, dw = torch.autograd.grad(yy, (zz, ww), g_y.to(yy.dtype))
     return dz, dw
 
 
 def _dz_total(ctx, g_z, g_y, z, t, c, dtype, device):
-    dz = g_z.contiguous().view(t, c).float() if g_z is not None else None
+    dz = g_z.contiguous().view(t, c) if g_z is not None else None
     dw = None
     if ctx.norm and g_y is not None:
         dzn, dw = _norm_bwd(g_y.contiguous().view(t, c), z, ctx.norm_w, ctx.norm_eps)
