@@ -344,6 +344,15 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
   float acc[RJ];
 #pragma unroll
   for (int q = 0; q < RJ; ++q) acc[q] = 0.f;
+  // this thread's phi column (k = kglob), the same for every tile: in
+  // registers for the usual projection widths, else read from shared memory
+  constexpr bool PREG = FD <= 32;
+  __syncthreads();
+  float pcol[PREG ? FD : 1];
+  if constexpr (PREG) {
+#pragma unroll
+    for (int j = 0; j < FD; ++j) pcol[j] = psT[j * KC + kk];
+  }
 
   for (int64_t tile = tile_beg; tile < tile_end; ++tile) {
     const int64_t t0 = tile * TT;
@@ -370,29 +379,52 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
       tgate[e] = tok < T ? gate_ws[t0 * N + e] : 0.f;
     }
     __syncthreads();
-    // dx for rows jgrp + JGRP*r, column kk
+    // dx for rows jgrp + JGRP*r, column kk.  Every global load of the tile's
+    // rows is issued before the arithmetic, so their latencies overlap.
     if (kvalid) {
+      float dzv[RR], dav[RR];
+#pragma unroll
+      for (int r = 0; r < RR; ++r) {
+        const int64_t tok = t0 + jgrp + JGRP * r;
+        dzv[r] = tok < T ? to_f(dz[tok * C + cc]) : 0.f;
+        dav[r] = (dx_add && tok < T) ? to_f(dx_add[tok * nC + kglob]) : 0.f;
+      }
 #pragma unroll
       for (int r = 0; r < RR; ++r) {
         const int row = jgrp + JGRP * r;
         const int64_t tok = t0 + row;
         if (tok >= T) continue;
         float a = 0.f;
+        if constexpr (!PREG) {
 #pragma unroll 8
-        for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
+          for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
+        } else if constexpr (FD % 4 == 0) {
+#pragma unroll
+          for (int j = 0; j < FD; j += 4) {
+            const float4 d4 = *reinterpret_cast<const float4 *>(dms + row * FD + j);  // one row: broadcast
+            a = fmaf(d4.x, pcol[j], a);
+            a = fmaf(d4.y, pcol[j + 1], a);
+            a = fmaf(d4.z, pcol[j + 2], a);
+            a = fmaf(d4.w, pcol[j + 3], a);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], pcol[j], a);
+        }
         float v = tinv[row] * a - trow[row] * xs[row * XSW + kk];
-        v = fmaf(tgate[row * N + stream_i], to_f(dz[tok * C + cc]), v);
-        if (dx_add) v += to_f(dx_add[tok * nC + kglob]);
+        v = fmaf(tgate[row * N + stream_i], dzv[r], v);
+        v += dav[r];
         dx[tok * nC + kglob] = from_f<Tx>(v);
       }
     }
-    // dphi[k, j] += sum_t (x * inv)[t, k] * dm[t, j]
+    // dphi[k, j] += sum_t (x * inv)[t, k] * dm[t, j] for this thread's
+    // consecutive columns j = jgrp * RJ + q
 #pragma unroll 4
     for (int t = 0; t < TT; ++t) {
       const float xn = xs[t * XSW + kk] * tinv[t];
 #pragma unroll
       for (int q = 0; q < RJ; ++q) {
-        const int j = jgrp + JGRP * q;
+        const int j = jgrp * RJ + q;
         if (j < FD) acc[q] = fmaf(xn, dms[t * FD + j], acc[q]);
       }
     }
@@ -401,7 +433,7 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
     float *dst = dphi_part + ((int64_t)blockIdx.y * nC + kglob) * FD;
 #pragma unroll
     for (int q = 0; q < RJ; ++q) {
-      const int j = jgrp + JGRP * q;
+      const int j = jgrp * RJ + q;
       if (j < FD) dst[j] = acc[q];
     }
   }
