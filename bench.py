@@ -396,8 +396,16 @@ def _layer_entry(lb, world, dev, steps, warmup, stream, peak, flush, with_bwd, s
         if lb.L.mhc_last_path() == 2:
             alt_pre = p_ms
         lb.L.mhc_set_path_policy(prev)
+    gen_pre = None
+    if lb.pre_path == lb.nat.RAN_FP32_STREAM:
+        # the fp32-stream tensor-core kernel ran: the generic CUDA-core pre beside it
+        prev = lb.L.mhc_set_path_policy(lb.nat.PATH_GENERIC)
+        _, (p_ms,) = _time_steps([lb.pre], steps, warmup, stream, fl)
+        if lb.L.mhc_last_path() == 0:
+            gen_pre = p_ms
+        lb.L.mhc_set_path_policy(prev)
     e = {"tokens_per_gpu": t, "tokens_per_s": world * t / (f_ms / 1e3), "ms_per_step": f_ms,
-         "pre_single_read_ms": alt_pre,
+         "pre_single_read_ms": alt_pre, "pre_generic_ms": gen_pre,
          "algorithmic_bytes_per_token": fb, "hbm_gbs_per_gpu": fb * t / (f_ms / 1e3) / 1e9,
          "frac_of_measured": fb * t / (f_ms / 1e3) / 1e9 / peak,
          "per_call_ms": {"pre": pre_ms, "post": post_ms}, "pre_path": lb.pre_path,

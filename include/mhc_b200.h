@@ -317,7 +317,10 @@ int mhc_device_sm_count(void);
 int mhc_set_path_policy(int policy);
 
 /* Kernel the process's last mhc_pre_fwd / mhc_head_fwd / mhc_post_pre_fwd ran
- * (on any thread: autograd runs backward on a thread of its own): 3 the fused
+ * (on any thread: autograd runs backward on a thread of its own): 4 the
+ * fp32-stream sm_100a coefficient kernel (fp32 x, n in {2, 4}, full or
+ * no-H_res, C a multiple of 128 with 4 <= C/128 <= 8, 16-byte aligned x and
+ * z; every policy but MHC_PATH_GENERIC), 3 the fused
  * merge + coefficient sm_100a kernel, 2 the single-read sm_100a kernel, 1 the
  * two-read sm_100a kernel, 0 the generic kernels; after
  * mhc_pre_bwd / mhc_head_bwd: 1 if the tensor-core dx / dphi kernel ran, 0

@@ -200,6 +200,16 @@ int mhc_pre_fwd(const void *x, int x_dtype, int64_t T, int n, int C, const void 
     if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_pre_fwd fused");
     cudaGetLastError();  // not supported on this device: generic kernels below
   }
+  if (g_policy != MHC_PATH_GENERIC && pre_xf_eligible(mode, n, x_dtype, x, z, T, C)) {
+    cudaError_t e = launch_pre_xf(mode, n, x, T, C, phi, p, z, h_pre, h_post, with_res ? h_res : nullptr,
+                                  coef_dtype, inv_rms, mixes, s);
+    if (e == cudaSuccess) {
+      g_last_path = 4;
+      return MHC_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "mhc_pre_fwd fp32 stream");
+    cudaGetLastError();  // not supported on this device: generic kernels below
+  }
   MHC_TRY(cuda_status(launch_coef_fwd(mode, n, x_dtype, x, T, C, phi, p, h_pre, h_post,
                                       with_res ? h_res : nullptr, coef_dtype, inv_rms, mixes, gate,
                                       device_sm_count(), s),

@@ -45,6 +45,17 @@
 //               reads them back) and frees the slots once the stores have
 //               read them.
 //
+// fp32 streams (XF; coefficient pass only, no merge or norm): the residual
+// stream of the reference's bf16-autocast trainers.  A ring slot holds 128
+// tokens x 32 fp32 columns (128-byte rows, 128-byte swizzle, 16 KB); warps
+// 16-19 (thread = token row) read their row, sum its squares in fp32 and
+// write it back over itself as [bf16 hi (32) | bf16 lo (32)], hi = rn(x),
+// lo = rn(x - hi): the same 128 bytes of the same row, so no other thread's
+// data is touched.  The MMA then reads the row as 64 bf16 K values, the hi
+// half and the lo half each against the 32 phi rows of the chunk:
+// (x_hi + x_lo) . (phi_hi + phi_lo), x to 2^-17 like phi.  z is accumulated
+// in fp32 from the fp32 x read back from L2 and written as fp32.
+//
 // Every hand-off is an mbarrier and every wait is bounded (mhc_sm100.cuh): a
 // wait that gives up sets the device error word, poisons the CTA's share of
 // the outputs with NaN and exits after draining its asynchronous work.
@@ -74,6 +85,7 @@ constexpr int COLS = 128;            // columns of every stream owned by a CTA
 constexpr int QC = 32;               // columns per chunk (a quarter of the CTA's 128)
 constexpr int NQ = COLS / QC;        // quarters per tile
 constexpr int CHUNK = TM * QC * 2;   // one ring slot: 128 rows x 32 bf16, 64-byte swizzle
+constexpr int CHUNK_F = TM * QC * 4; // fp32 streams: 128 rows x 32 fp32, 128-byte swizzle
 constexpr int RING_MAX = 24;
 constexpr int S_MIN = 4, S_MAX = 8;  // cluster sizes (C = 128 S)
 constexpr int TPC_MAX = 32;          // tokens a CTA owns per tile: ceil(128 / S)
@@ -86,9 +98,10 @@ constexpr int XSB = 4;               // "x' of tile stored" barriers
 constexpr int MGB = 6;               // "merged quarter ready" barriers
 constexpr int ACC_STRIDE = 256, TMEM_COLS = 512, GRAM = 64;
 
-template <bool MERGE>
+// warps 16-19 exist with a merge (merge warps) and for fp32 streams (convert warps)
+template <bool CONV>
 struct Warps {
-  static constexpr int NWARPS = MERGE ? W_MRG + NMW : W_MRG;
+  static constexpr int NWARPS = CONV ? W_MRG + NMW : W_MRG;
   static constexpr int NTHREADS = NWARPS * 32;
 };
 
@@ -115,11 +128,11 @@ struct Layout {
   uint32_t ring, phi, inbox, hp, lg, zss, nw, ssb, par, bar, tmem, abort, total;
 };
 
-__host__ __device__ inline Layout make_layout(int RING, int CH, int NB, int IBS, int HPN, int NPAR, int S, int TPC,
-                                              int norm) {
+__host__ __device__ inline Layout make_layout(int RING, int SLOT, int CH, int NB, int IBS, int HPN, int NPAR, int S,
+                                              int TPC, int norm) {
   Layout L;
   uint32_t o = 0;
-  L.ring = o;  o += (uint32_t)RING * CHUNK;
+  L.ring = o;  o += (uint32_t)RING * SLOT;
   L.phi = o;   o += (uint32_t)CH * NB * 64;
   L.inbox = o; o += (uint32_t)S * TPC * IBS * 4;
   L.hp = o;    o += (uint32_t)HB * TM * HPN * 4;
@@ -140,12 +153,13 @@ struct Args {
   int C, nC, S, TPC, RING;
   const void *phi;
   CoefParams p;
-  const __nv_bfloat16 *xz;   // what the pre-aggregate reads: x' (merge) or x
+  const void *xz;            // what the pre-aggregate reads: x' (merge) or x (bf16, or fp32 for XF)
   __nv_bfloat16 *x_out;      // x' (merge), for poisoning
   const void *hres_prev;     // merge coefficients of the previous sublayer (NULL: H_res = I)
   const void *hpost_prev;
   int prev_dtype;
-  __nv_bfloat16 *z, *y;      // pre-aggregate and its RMSNorm (y may be NULL)
+  void *z;                   // pre-aggregate (x's dtype)
+  __nv_bfloat16 *y;          // its RMSNorm (may be NULL)
   const void *norm_w;
   int norm_dtype;
   float norm_eps;
@@ -182,7 +196,7 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // After a wait gave up the CTA overwrites its share of every tile of its
 // cluster with NaN: its 128 columns of z, y and x' and the per-token outputs
 // of the tokens it owns.
-template <int N, int MODE>
+template <int N, int MODE, bool XF>
 __device__ void poison_share(const Args &a, int cid, int ncl, int rank, int ntiles, int tid, int nthreads) {
   constexpr int FD = Dims<N, MODE>::FD;
   const float qnan = __int_as_float(0x7fc00000);
@@ -193,7 +207,8 @@ __device__ void poison_share(const Args &a, int cid, int ncl, int rank, int ntil
     const int rows = a.T - t0 < TM ? (int)(a.T - t0) : TM;
     for (int e = tid; e < rows * COLS; e += nthreads) {
       const int r = e / COLS, c = e - r * COLS;
-      a.z[(t0 + r) * a.C + c0 + c] = bnan;
+      if (XF) reinterpret_cast<float *>(a.z)[(t0 + r) * a.C + c0 + c] = qnan;
+      else reinterpret_cast<__nv_bfloat16 *>(a.z)[(t0 + r) * a.C + c0 + c] = bnan;
       if (a.y) a.y[(t0 + r) * a.C + c0 + c] = bnan;
       if (a.x_out)
         for (int i = 0; i < N; ++i) a.x_out[(t0 + r) * a.nC + i * a.C + c0 + c] = bnan;
@@ -232,21 +247,24 @@ __device__ __forceinline__ void load_params(float *par, const CoefParams &p, int
   }
 }
 
-template <int N, int MODE, bool MERGE, bool NORM>
-__global__ void __launch_bounds__(Warps<MERGE>::NTHREADS, 1)
+template <int N, int MODE, bool MERGE, bool NORM, bool XF>
+__global__ void __launch_bounds__(Warps<MERGE || XF>::NTHREADS, 1)
 post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmf,
                 const __grid_constant__ CUtensorMap tmo, Args a) {
+  static_assert(!(XF && (MERGE || NORM)), "fp32 streams: coefficient pass only");
   using Cf = Cfg<N, MODE>;
   constexpr int FD = Cf::FD, NB = Cf::NB, IBS = Cf::IBS, NPAR = Cf::NPAR, HPN = Cf::HPN, CH = Cf::CH;
-  constexpr int NTHREADS = Warps<MERGE>::NTHREADS, NWARPS = Warps<MERGE>::NWARPS;
+  constexpr bool CONV = MERGE || XF;     // warps 16-19 rewrite the ring slots before the MMA
+  constexpr int NTHREADS = Warps<CONV>::NTHREADS, NWARPS = Warps<CONV>::NWARPS;
   constexpr int NCONV = NWARPS - W_CONV;
   constexpr int NL = MERGE ? N + 1 : N;  // ring slots per quarter (x chunks, then f)
+  constexpr uint32_t SLOT = XF ? CHUNK_F : CHUNK;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
   uint8_t *base = smem_raw + (base_u32 - raw_u32);
   const int S = a.S, TPC = a.TPC, RING = a.RING;
-  const Layout L = make_layout(RING, CH, NB, IBS, HPN, NPAR, S, TPC, NORM ? 1 : 0);
+  const Layout L = make_layout(RING, SLOT, CH, NB, IBS, HPN, NPAR, S, TPC, NORM ? 1 : 0);
   float *inbox = reinterpret_cast<float *>(base + L.inbox);
   float *hp = reinterpret_cast<float *>(base + L.hp);
   float *lg = reinterpret_cast<float *>(base + L.lg);
@@ -293,13 +311,13 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
       mbar_init(BAR(B_LGF + b), 1);
       mbar_init(BAR(B_LGE + b), 1);
     }
-    for (int b = 0; b < MGB; ++b) mbar_init(BAR(B_MRG + b), NMW);  // one per merge warp
+    for (int b = 0; b < MGB; ++b) mbar_init(BAR(B_MRG + b), NMW);  // one per merge / convert warp
     for (int b = 0; b < XSB; ++b) {
       mbar_init(BAR(B_XSF + b), 1);        // x' of the tile complete in global memory
       mbar_init(BAR(B_XSE + b), 1);        // coefficient warp saw it
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(BAR(B_SSF + b), NMW);      // merge warps wrote the tile's sums of squares
+      mbar_init(BAR(B_SSF + b), NMW);      // merge / convert warps wrote the tile's sums of squares
       mbar_init(BAR(B_SSE + b), 4);        // row warps read them
     }
     mbar_init(BAR(B_DRAIN), 1);
@@ -382,8 +400,8 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
           for (int i = 0; i < NL; ++i, ++q) {
             const uint32_t slot = q % RING, ph = (q / RING) & 1u;
             if (!wait_parity<false>(BAR(B_EMPTY + slot), ph ^ 1u, abort_flag)) { ok = false; break; }
-            mbar_arrive_expect_tx(BAR(B_FULL + slot), CHUNK);
-            const uint32_t dst = base_u32 + L.ring + slot * CHUNK;
+            mbar_arrive_expect_tx(BAR(B_FULL + slot), SLOT);
+            const uint32_t dst = base_u32 + L.ring + slot * SLOT;
             if (i < N) tma_load_2d_hint(dst, &tmx, i * a.C + c0 + qq * QC, tile * TM, BAR(B_FULL + slot), xpol);
             else tma_load_2d_hint(dst, &tmf, c0 + qq * QC, tile * TM, BAR(B_FULL + slot), fpol);
           }
@@ -411,27 +429,37 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)buf * ACC_STRIDE;
         for (int qq = 0; qq < NQ && ok; ++qq, ++hq) {
-          if (MERGE) {
-            // the merge warps formed this quarter's x' chunks in place
+          if (CONV) {
+            // the merge warps formed this quarter's x' chunks in place (fp32
+            // streams: the convert warps split them into bf16 hi | lo)
             if (!wait_parity<false>(BAR(B_MRG + hq % MGB), (hq / MGB) & 1u, abort_flag)) { ok = false; break; }
             tc_fence_after();
           }
           for (int i = 0; i < NL; ++i, ++q) {
             const uint32_t slot = q % RING, ph = (q / RING) & 1u;
             if (i == N) continue;  // the f chunk: the store warp frees it
-            if (!MERGE) {
+            if (!CONV) {
               if (!wait_parity<false>(BAR(B_FULL + slot), ph, abort_flag)) { ok = false; break; }
               tc_fence_after();
             }
-            const uint32_t a0 = base_u32 + L.ring + slot * CHUNK;
+            const uint32_t a0 = base_u32 + L.ring + slot * SLOT;
             const uint32_t b0 = base_u32 + L.phi + (uint32_t)(i * NQ + qq) * NB * 64u;
+            if constexpr (XF) {
+              // 128-byte rows [hi k0..31 | lo k0..31]: K steps 0-1 the hi
+              // half, 2-3 the lo half, each against phi rows k0..31
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const uint64_t ad = umma_desc_sw64(a0 + k * 32);
-              const uint32_t accum = (qq | i | k) != 0 ? 1u : 0u;
-              umma_bf16(dcol, ad, umma_desc_sw64(b0 + k * 32), idesc, accum);
-              // sum of squares of each row = diagonal of x . x^T
-              if (!MERGE) umma_bf16(dcol + GRAM, ad, ad, gdesc, accum);
+              for (int k = 0; k < 4; ++k)
+                umma_bf16(dcol, umma_desc_sw128(a0 + k * 32), umma_desc_sw64(b0 + (k & 1) * 32), idesc,
+                          (qq | i | k) != 0 ? 1u : 0u);
+            } else {
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const uint64_t ad = umma_desc_sw64(a0 + k * 32);
+                const uint32_t accum = (qq | i | k) != 0 ? 1u : 0u;
+                umma_bf16(dcol, ad, umma_desc_sw64(b0 + k * 32), idesc, accum);
+                // sum of squares of each row = diagonal of x . x^T
+                if (!MERGE) umma_bf16(dcol + GRAM, ad, ad, gdesc, accum);
+              }
             }
             umma_commit(BAR(B_EMPTY + slot));
           }
@@ -442,10 +470,10 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
 #pragma unroll
             for (int i = 0; i < N; ++i) {
 #if MHC_CH_STORE_HINT
-              tma_store_2d_hint(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * CHUNK, i * a.C + c0 + qq * QC,
+              tma_store_2d_hint(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * SLOT, i * a.C + c0 + qq * QC,
                                 tile * TM, opol);
 #else
-              tma_store_2d(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * CHUNK, i * a.C + c0 + qq * QC, tile * TM);
+              tma_store_2d(&tmo, base_u32 + L.ring + ((q0 + i) % RING) * SLOT, i * a.C + c0 + qq * QC, tile * TM);
 #endif
             }
             bulk_commit();
@@ -499,7 +527,7 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
         for (int i = 0; i < 16; ++i) d[c16 * 16 + i] = t16[i];
       }
       float ss = 0.f;
-      if constexpr (!MERGE) {
+      if constexpr (!CONV) {
         // Gram diagonal: this lane's row is column quad*32 + lane of the block
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -512,8 +540,8 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(B_ACCE + buf));
-      if constexpr (MERGE) {
-        // the merge warps' sum of squares of the row
+      if constexpr (CONV) {
+        // the merge / convert warps' sum of squares of the row
         if (!WAIT_WARP(false, BAR(B_SSF + buf), aph)) { ok = false; break; }
         ss = ssb[buf * TM + row];
         __syncwarp();
@@ -651,7 +679,9 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
     // ---------------- pre-aggregate warps ----------------
     // thread = (vector v of 8 columns, rows r0 + 16u, u < 8): 128 rows x 16
     // vectors over 256 threads; a row's 16 vectors are one half-warp.
-    constexpr int IPT = 8, IPB = NORM ? 2 : 4;  // items per thread, items per batch of loads
+    // (fp32 streams: an item is 8 fp32 columns, two 16-byte vectors per stream)
+    constexpr int IPT = 8, IPB = (NORM || XF) ? 2 : 4;  // items per thread, items per batch of loads
+    constexpr int XV = XF ? 2 : 1;                      // 16-byte vectors per stream and item
     const int ztid = tid - W_Z * 32;
     const int v = ztid & 15, r0 = ztid >> 4;
     int lt = 0;
@@ -667,21 +697,25 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
       if (!WAIT_WARP(false, BAR(B_ZGO + hb), hph)) { ok = false; break; }
       const int64_t t0 = (int64_t)tile * TM;
       const int rows = a.T - t0 < TM ? (int)(a.T - t0) : TM;
-      const __nv_bfloat16 *xb = a.xz + t0 * a.nC + c0 + v * 8;
-      __nv_bfloat16 *zb = a.z + t0 * a.C + c0 + v * 8;
+      constexpr int ES = XF ? 4 : 2;  // element bytes of x and z
+      const uint8_t *xb = reinterpret_cast<const uint8_t *>(a.xz) + (t0 * a.nC + c0 + v * 8) * ES;
+      uint8_t *zb = reinterpret_cast<uint8_t *>(a.z) + (t0 * a.C + c0 + v * 8) * ES;
       const float *hps = hp + hb * TM * HPN;
       uint4 zk[NORM ? IPT : 1];
       float ss[NORM ? IPT : 1];
 #pragma unroll
       for (int b = 0; b < IPT / IPB; ++b) {
-        uint4 xv[IPB][N];
+        uint4 xv[IPB][N][XV];
 #pragma unroll
         for (int u = 0; u < IPB; ++u) {
           const int r = r0 + 16 * (b * IPB + u);
           if (r < rows) {
 #pragma unroll
             for (int st = 0; st < N; ++st)
-              xv[u][st] = __ldcs(reinterpret_cast<const uint4 *>(xb + (int64_t)r * a.nC + st * a.C));
+#pragma unroll
+              for (int h = 0; h < XV; ++h)
+                xv[u][st][h] = __ldcs(
+                    reinterpret_cast<const uint4 *>(xb + ((int64_t)r * a.nC + st * a.C) * ES + h * 16));
           }
         }
         if (b == 0) {
@@ -703,22 +737,39 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
 #pragma unroll
             for (int st = 0; st < N; ++st) {
               const uint64_t w2 = f2_pack(wv[st], wv[st]);
-              const uint32_t xw[4] = {xv[u][st].x, xv[u][st].y, xv[u][st].z, xv[u][st].w};
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                acc[j] = st == 0 ? f2_fma(w2, bf16x2_to_f2(xw[j]), f2_pack(0.f, 0.f))
-                                 : f2_fma(w2, bf16x2_to_f2(xw[j]), acc[j]);
+              for (int j = 0; j < 4; ++j) {
+                uint64_t xp;
+                if constexpr (XF) {
+                  const uint4 q4 = xv[u][st][j >> 1];
+                  xp = (j & 1) ? f2_pack(__uint_as_float(q4.z), __uint_as_float(q4.w))
+                               : f2_pack(__uint_as_float(q4.x), __uint_as_float(q4.y));
+                } else {
+                  const uint32_t xw[4] = {xv[u][st][0].x, xv[u][st][0].y, xv[u][st][0].z, xv[u][st][0].w};
+                  xp = bf16x2_to_f2(xw[j]);
+                }
+                acc[j] = st == 0 ? f2_fma(w2, xp, f2_pack(0.f, 0.f)) : f2_fma(w2, xp, acc[j]);
+              }
             }
-            uint32_t ow[4];
+            uint8_t *zr = zb + (int64_t)r * a.C * ES;
+            if constexpr (XF) {
+              float o[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float lo, hi;
-              f2_unpack(acc[j], lo, hi);
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
-              ow[j] = *reinterpret_cast<const uint32_t *>(&h2);
+              for (int j = 0; j < 4; ++j) f2_unpack(acc[j], o[2 * j], o[2 * j + 1]);
+              reinterpret_cast<float4 *>(zr)[0] = make_float4(o[0], o[1], o[2], o[3]);
+              reinterpret_cast<float4 *>(zr)[1] = make_float4(o[4], o[5], o[6], o[7]);
+            } else {
+              uint32_t ow[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float lo, hi;
+                f2_unpack(acc[j], lo, hi);
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+                ow[j] = *reinterpret_cast<const uint32_t *>(&h2);
+              }
+              out = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+              *reinterpret_cast<uint4 *>(zr) = out;
             }
-            out = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-            *reinterpret_cast<uint4 *>(zb + (int64_t)r * a.C) = out;
           }
           if constexpr (NORM) {
             // the row's sum of squares over this vector, of the bf16 z values
@@ -869,6 +920,65 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
       if (lane == 0) mbar_arrive(BAR(B_SSF + sb));
     }
     if (!ok) record_error(ERR_MRG, abort_flag, a.err_flag);
+  } else if (XF && warp >= W_MRG && warp < W_MRG + NMW) {
+    // ---------------- convert warps (fp32 streams) ----------------
+    // Row `row` of a slot is 128 bytes: 32 fp32 in 16-byte granules g at
+    // granule position g ^ (row & 7).  It is rewritten as 64 bf16, hi of the
+    // 32 values in granules 0-3 and lo in granules 4-7 (same swizzle), which
+    // the MMA reads as one 128-byte K-major row.
+    const int row = tid - W_MRG * 32;
+    const uint32_t r7 = (uint32_t)(row & 7);
+    uint32_t q = 0, hq = 0;
+    bool ok = true;
+    int lt = 0;
+    for (int tile = (int)cid; tile < ntiles && ok; tile += (int)ncl, ++lt) {
+      uint64_t ss2 = f2_pack(0.f, 0.f);  // sum of squares of the row (column pairs)
+      for (int qq = 0; qq < NQ; ++qq, ++hq) {
+#pragma unroll 1
+        for (int i = 0; i < N; ++i, ++q) {
+          const uint32_t sl = q % RING;
+          if (!WAIT_WARP(false, BAR(B_FULL + sl), (q / RING) & 1u)) { ok = false; break; }
+          uint8_t *rp = base + L.ring + sl * SLOT + (uint32_t)row * 128u;
+          float4 xv[8];
+#pragma unroll
+          for (int g = 0; g < 8; ++g) xv[g] = *reinterpret_cast<const float4 *>(rp + ((((uint32_t)g) ^ r7) << 4));
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float e[8] = {xv[2 * h].x, xv[2 * h].y, xv[2 * h].z, xv[2 * h].w,
+                                xv[2 * h + 1].x, xv[2 * h + 1].y, xv[2 * h + 1].z, xv[2 * h + 1].w};
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              const __nv_bfloat162 hi2 = __floats2bfloat162_rn(e[2 * p], e[2 * p + 1]);
+              const float2 hf = __bfloat1622float2(hi2);
+              const __nv_bfloat162 lo2 = __floats2bfloat162_rn(e[2 * p] - hf.x, e[2 * p + 1] - hf.y);
+              hw[p] = *reinterpret_cast<const uint32_t *>(&hi2);
+              lw[p] = *reinterpret_cast<const uint32_t *>(&lo2);
+              const uint64_t x2 = f2_pack(e[2 * p], e[2 * p + 1]);
+              ss2 = f2_fma(x2, x2, ss2);
+            }
+            *reinterpret_cast<uint4 *>(rp + ((((uint32_t)h) ^ r7) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(rp + ((((uint32_t)(4 + h)) ^ r7) << 4)) =
+                make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          }
+        }
+        if (!ok) break;
+        fence_proxy_async_smem();  // generic hi | lo writes -> MMA (async proxy) reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(B_MRG + hq % MGB));
+      }
+      if (!ok) break;
+      // the row's sum of squares for the row warps (buffer free once they
+      // read the tile two back)
+      const int sb = lt & 1;
+      if (!WAIT_WARP(false, BAR(B_SSE + sb), ((uint32_t)(lt >> 1) & 1u) ^ 1u)) { ok = false; break; }
+      float slo, shi;
+      f2_unpack(ss2, slo, shi);
+      ssb[sb * TM + row] = slo + shi;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(B_SSF + sb));
+    }
+    if (!ok) record_error(ERR_MRG, abort_flag, a.err_flag);
   }
 
   // ---------------- teardown ----------------
@@ -877,7 +987,7 @@ post_pre_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
-  if (*abort_flag) poison_share<N, MODE>(a, (int)cid, (int)ncl, (int)rank, ntiles, tid, NTHREADS);
+  if (*abort_flag) poison_share<N, MODE, XF>(a, (int)cid, (int)ncl, (int)rank, ntiles, tid, NTHREADS);
   cluster_sync_all();  // no CTA leaves while a peer may still touch its shared memory
 #undef WAIT_WARP
 #undef BAR
@@ -910,29 +1020,35 @@ constexpr size_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per block
 // The longest ring that fits the shared-memory budget, at least `need` slots
 // (merge: one column half = n + 1 chunks; at most MGB halves so that a
 // "merged half" barrier is never two phases ahead of its waiters).
-template <int N, int MODE, bool MERGE, bool NORM>
+template <int N, int MODE, bool MERGE, bool NORM, bool XF>
 static int pick_ring(int S, int TPC) {
   using Cf = Cfg<N, MODE>;
-  const int need = MERGE ? N + 1 : 3;
-  const int cap = MERGE ? (MGB * (N + 1) < RING_MAX ? MGB * (N + 1) : RING_MAX) : RING_MAX;
+  const int slot = XF ? CHUNK_F : CHUNK;
+  const int need = MERGE ? N + 1 : (XF ? N : 3);
+  // merge / convert: the warps 16-19 run at most RING / quarter ahead of the
+  // MMA issuer, which must stay under MGB quarters
+  const int cap = MERGE ? (MGB * (N + 1) < RING_MAX ? MGB * (N + 1) : RING_MAX)
+                        : (XF ? ((MGB - 1) * N < RING_MAX ? (MGB - 1) * N : RING_MAX) : RING_MAX);
   for (int r = cap; r >= need; --r)
-    if ((size_t)make_layout(r, Cf::CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, S, TPC, NORM ? 1 : 0).total + 1024 <=
+    if ((size_t)make_layout(r, slot, Cf::CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, S, TPC, NORM ? 1 : 0).total + 1024 <=
         SMEM_LIMIT)
       return r;
   return 0;
 }
 
-// a (rows x cols) row-major bf16 matrix in 128-row x 32-column boxes with a
-// 64-byte swizzle (the MMA's K-major operand layout for 64-byte rows)
-static bool encode_2d(CUtensorMap &m, const void *p, int64_t rows, int64_t cols) {
+// a (rows x cols) row-major matrix in 128-row x 32-column boxes: bf16 with a
+// 64-byte swizzle (the MMA's K-major operand layout for 64-byte rows), fp32
+// with a 128-byte swizzle (128-byte rows)
+static bool encode_2d(CUtensorMap &m, const void *p, int64_t rows, int64_t cols, bool f32 = false) {
   auto enc = encode_fn();
   if (!enc) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * (f32 ? 4 : 2)};
   const cuuint32_t box[2] = {(cuuint32_t)QC, (cuuint32_t)TM};
   const cuuint32_t estr[2] = {1, 1};
-  return enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(p), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return enc(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(p),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -947,14 +1063,15 @@ static std::mutex g_mu;
 static KernEntry g_kerns[64];
 static int g_kerns_n = 0;
 
-template <int N, int MODE, bool MERGE, bool NORM>
+template <int N, int MODE, bool MERGE, bool NORM, bool XF = false>
 static cudaError_t launch_impl(const void *x, const void *f, Args a, cudaStream_t stream) {
   using Cf = Cfg<N, MODE>;
-  a.RING = pick_ring<N, MODE, MERGE, NORM>(a.S, a.TPC);
+  a.RING = pick_ring<N, MODE, MERGE, NORM, XF>(a.S, a.TPC);
   if (a.RING == 0) return cudaErrorNotSupported;
-  const size_t smem =
-      (size_t)make_layout(a.RING, Cf::CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR, a.S, a.TPC, NORM ? 1 : 0).total + 1024;
-  auto kern = post_pre_kernel<N, MODE, MERGE, NORM>;
+  const size_t smem = (size_t)make_layout(a.RING, XF ? CHUNK_F : CHUNK, Cf::CH, Cf::NB, Cf::IBS, Cf::HPN, Cf::NPAR,
+                                          a.S, a.TPC, NORM ? 1 : 0).total +
+                      1024;
+  auto kern = post_pre_kernel<N, MODE, MERGE, NORM, XF>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -969,7 +1086,7 @@ static cudaError_t launch_impl(const void *x, const void *f, Args a, cudaStream_
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;  // cluster shape only for the occupancy query
-  cfg.blockDim = dim3(Warps<MERGE>::NTHREADS, 1, 1);
+  cfg.blockDim = dim3(Warps<MERGE || XF>::NTHREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
 
@@ -995,7 +1112,7 @@ static cudaError_t launch_impl(const void *x, const void *f, Args a, cudaStream_
   }
 
   CUtensorMap tmx, tmf, tmo;
-  if (!encode_2d(tmx, x, a.T, a.nC)) return cudaErrorNotSupported;
+  if (!encode_2d(tmx, x, a.T, a.nC, XF)) return cudaErrorNotSupported;
   if (MERGE) {
     if (!encode_2d(tmf, f, a.T, a.C)) return cudaErrorNotSupported;
     if (!encode_2d(tmo, a.x_out, a.T, a.nC)) return cudaErrorNotSupported;
@@ -1043,12 +1160,12 @@ cudaError_t launch_post_pre(int mode, int n, const void *x, const void *f, const
   a.p = p;
   const bool merge = f != nullptr;
   const bool norm = norm_w != nullptr;
-  a.xz = reinterpret_cast<const __nv_bfloat16 *>(merge ? x_out : x);
+  a.xz = merge ? x_out : x;
   a.x_out = merge ? reinterpret_cast<__nv_bfloat16 *>(x_out) : nullptr;
   a.hres_prev = h_res_prev;
   a.hpost_prev = h_post_prev;
   a.prev_dtype = prev_dtype;
-  a.z = reinterpret_cast<__nv_bfloat16 *>(z);
+  a.z = z;
   a.y = norm ? reinterpret_cast<__nv_bfloat16 *>(y) : nullptr;
   a.norm_w = norm_w;
   a.norm_dtype = norm_dtype;
@@ -1074,6 +1191,46 @@ cudaError_t launch_post_pre(int mode, int n, const void *x, const void *f, const
       };
       if (n == 2) return go(std::integral_constant<int, 2>{});
       if (n == 4) return go(std::integral_constant<int, 4>{});
+    }
+    return cudaErrorNotSupported;
+  });
+}
+
+bool pre_xf_eligible(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C) {
+  if (x_dtype != MHC_F32 || T < 1) return false;
+  if (mode != FULL && mode != NOHRES) return false;
+  if (n != 2 && n != 4) return false;
+  if (C % ch::COLS != 0) return false;
+  const int S = C / ch::COLS;
+  if (S < ch::S_MIN || S > ch::S_MAX) return false;
+  return ((uintptr_t)x & 15) == 0 && ((uintptr_t)z & 15) == 0;
+}
+
+cudaError_t launch_pre_xf(int mode, int n, const void *x, int64_t T, int C, const void *phi, const CoefParams &p,
+                          void *z, void *h_pre, void *h_post, void *h_res, int coef_dtype, float *inv_rms,
+                          float *mixes, cudaStream_t stream) {
+  ch::Args a = {};
+  a.T = T;
+  a.C = C;
+  a.nC = n * C;
+  a.S = C / ch::COLS;
+  a.TPC = (ch::TM + a.S - 1) / a.S;
+  a.phi = phi;
+  a.p = p;
+  a.xz = x;
+  a.z = z;
+  a.h_pre = h_pre;
+  a.h_post = h_post;
+  a.h_res = h_res;
+  a.coef_dtype = coef_dtype;
+  a.inv_rms = inv_rms;
+  a.mixes = mixes;
+  a.err_flag = host_error_flag();
+  return with_mode(mode, [&](auto md) -> cudaError_t {
+    constexpr int MODE = decltype(md)::value;
+    if constexpr (MODE == FULL || MODE == NOHRES) {
+      if (n == 2) return ch::launch_impl<2, MODE, false, false, true>(x, nullptr, a, stream);
+      if (n == 4) return ch::launch_impl<4, MODE, false, false, true>(x, nullptr, a, stream);
     }
     return cudaErrorNotSupported;
   });

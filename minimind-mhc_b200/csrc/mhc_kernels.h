@@ -65,6 +65,12 @@ cudaError_t launch_post_pre(int mode, int n, const void *x, const void *f, const
                             const void *phi, const CoefParams &p, void *z, void *h_pre, void *h_post,
                             void *h_res, int coef_dtype, float *inv_rms, float *mixes, const void *norm_w,
                             int norm_dtype, float norm_eps, void *y, cudaStream_t stream);
+// the same kernel's coefficient pass for fp32 activations (z fp32): x split
+// into bf16 hi | lo in shared memory for the tensor-core projection
+bool pre_xf_eligible(int mode, int n, int x_dtype, const void *x, const void *z, int64_t T, int C);
+cudaError_t launch_pre_xf(int mode, int n, const void *x, int64_t T, int C, const void *phi, const CoefParams &p,
+                          void *z, void *h_pre, void *h_post, void *h_res, int coef_dtype, float *inv_rms,
+                          float *mixes, cudaStream_t stream);
 int read_ch_error(bool clear);
 cudaError_t launch_rmsnorm_rows(int z_dtype, const void *z, const void *w, int w_dtype, float eps, void *y,
                                 int64_t T, int C, cudaStream_t stream);

@@ -65,7 +65,7 @@ _PROTOS = {
 
 PATH_AUTO, PATH_GENERIC, PATH_TWO_READ, PATH_SINGLE_READ, PATH_FUSED_POST_PRE = 0, 1, 2, 3, 4
 # mhc_last_path() after a forward call: the kernel family that ran
-RAN_GENERIC, RAN_TWO_READ, RAN_SINGLE_READ, RAN_POST_PRE = 0, 1, 2, 3
+RAN_GENERIC, RAN_TWO_READ, RAN_SINGLE_READ, RAN_POST_PRE, RAN_FP32_STREAM = 0, 1, 2, 3, 4
 
 EXPORTED = tuple(_PROTOS)
 
