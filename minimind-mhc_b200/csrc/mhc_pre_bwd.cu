@@ -12,9 +12,13 @@
 //     the workspace.  (Without K1a's dots it computes them itself, one warp per
 //     token.)
 //  K2 dx_dphi_kernel   : grid (k-chunks x token splits).  For its k-chunk a block
-//     keeps phi^T in shared memory and, per 32-token tile,
-//       dx = inv*(dm @ phi^T) - rowb*x + w_i*dz + dx_add
-//     and accumulates dphi[k, :] += (x*inv)[t,k] * dm[t,:] in registers.
+//     keeps phi^T in shared memory and, per 32-token tile (dm scaled by the
+//     token's 1/rms when staged),
+//       dx = (inv*dm) @ phi^T - rowb*x + w_i*dz + dx_add
+//     and accumulates dphi[k, :] += x[t,k] * (inv*dm)[t,:] in registers
+//     (register-tiled: 2 columns x up to 16 projection columns per thread,
+//     the tile's tokens split over warp groups, whose partials are summed in
+//     a fixed order at the end).
 //  K3 reduce kernels   : fixed-order sums of the per-split dphi partials and of
 //     the per-block alpha / bias partials.
 #include "mhc_device.cuh"
@@ -295,30 +299,47 @@ coef_bwd_kernel(const Tx *__restrict__ x, int64_t T, int C, CoefParams p,
 // ---------------------------------------------------------------------------
 // K2
 // ---------------------------------------------------------------------------
+// Shared-memory floats the kernel below needs (the staging buffers, or the
+// dphi reduction over the token groups at the end, whichever is larger).
+template <int N, int MODE>
+struct DxDphiCfg {
+  static constexpr int FD = Dims<N, MODE>::FD;
+  static constexpr int KC = FD <= 96 ? 64 : 16;    // columns k per block
+  static constexpr int TT = 32;                    // tokens per tile
+  static constexpr int XSW = KC;                   // x tile row stride (floats)
+  // dphi register tiling (KC = 64): lane = column pair, warp = (j group, token group)
+  static constexpr bool RT = KC == 64;
+  static constexpr int JH = FD <= 16 ? 1 : (FD <= 32 ? 2 : (FD <= 64 ? 4 : 8));
+  static constexpr int JR = (FD + JH - 1) / JH;    // projection columns per thread
+  static constexpr int TG = 8 / JH;                // token groups
+  static constexpr int STAGE = FD * KC + TT * XSW + TT * FD + 2 * TT + TT * N;
+  static constexpr int FDP = FD + 1;              // reduction row stride (odd: fewer bank conflicts)
+  static constexpr int RED = RT ? TG * KC * FDP : 0;
+  static constexpr int SMEM_FLOATS = STAGE > RED ? STAGE : RED;
+};
+
 template <int N, int MODE, typename Tx>
 __global__ void __launch_bounds__(256)
 dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restrict__ phi, int pdt,
                const float *__restrict__ inv_rms, const float *__restrict__ dm_ws,
                const float *__restrict__ rowb_ws, const float *__restrict__ gate_ws,
                const Tx *__restrict__ dz, const Tx *__restrict__ dx_add, Tx *__restrict__ dx,
-               float *__restrict__ dphi_part, int tsplits) {
-  constexpr int FD = Dims<N, MODE>::FD;
-  constexpr int KC = FD <= 96 ? 64 : 16;
-  constexpr int JGRP = 256 / KC;               // j groups (dphi) / token rows (dx)
-  constexpr int RJ = (FD + JGRP - 1) / JGRP;
-  constexpr int TT = 32;                       // tokens per tile
+               float *__restrict__ dphi_part, int tsplits, bool xvec) {
+  using Cf = DxDphiCfg<N, MODE>;
+  constexpr int FD = Cf::FD, KC = Cf::KC, TT = Cf::TT, XSW = Cf::XSW;
+  constexpr int JGRP = 256 / KC;               // token rows of the dx pass per column
   constexpr int RR = TT / JGRP;                // dx rows per thread
-  constexpr int XSW = KC + 1;
+  constexpr int RJ = (FD + JGRP - 1) / JGRP;   // dphi columns per thread without the tiling
+  constexpr int JH = Cf::JH, JR = Cf::JR, TG = Cf::TG;
   extern __shared__ float4 smem4[];
   float *smem = reinterpret_cast<float *>(smem4);
   float *psT = smem;                  // [FD][KC]
   float *xs = psT + FD * KC;          // [TT][XSW]
-  float *dms = xs + TT * XSW;         // [TT][FD]
-  float *tinv = dms + TT * FD;        // [TT]
-  float *trow = tinv + TT;            // [TT]
-  float *tgate = trow + TT;           // [TT][N]
+  float *dms = xs + TT * XSW;         // [TT][FD]: inv * dm
+  float *trow = dms + TT * FD;        // [TT]
+  float *tgate = trow + 2 * TT;       // [TT][N]
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kk = tid % KC, jgrp = tid / KC;
   const int64_t nC = (int64_t)N * C;
   const int64_t k0 = (int64_t)blockIdx.x * KC;
@@ -326,6 +347,8 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
   const bool kvalid = kglob < nC;
   const int stream_i = kvalid ? (int)(kglob / C) : 0;
   const int cc = kvalid ? (int)(kglob - (int64_t)stream_i * C) : 0;
+  // dphi tiling: columns 2*lane, 2*lane+1; projection columns jh*JR + q; tokens tg + TG*u
+  const int jh = warp % JH, tg = warp / JH;
 
   for (int e = tid; e < KC * FD; e += blockDim.x) {
     const int r = e / FD, j = e - r * FD;
@@ -341,9 +364,9 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
   int64_t tile_end = tile_beg + tiles_per;
   if (tile_end > tiles) tile_end = tiles;
 
-  float acc[RJ];
+  float acc[Cf::RT ? 2 * JR : RJ];
 #pragma unroll
-  for (int q = 0; q < RJ; ++q) acc[q] = 0.f;
+  for (int q = 0; q < (Cf::RT ? 2 * JR : RJ); ++q) acc[q] = 0.f;
   // this thread's phi column (k = kglob), the same for every tile: in
   // registers for the usual projection widths, else read from shared memory
   constexpr bool PREG = FD <= 32;
@@ -357,21 +380,33 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
   for (int64_t tile = tile_beg; tile < tile_end; ++tile) {
     const int64_t t0 = tile * TT;
     __syncthreads();
-    for (int e = tid; e < TT * KC; e += blockDim.x) {
-      const int r = e / KC, c = e - r * KC;
-      const int64_t tok = t0 + r;
-      float v = 0.f;
-      if (tok < T && k0 + c < nC) v = to_f(x[tok * nC + k0 + c]);
-      xs[r * XSW + c] = v;
+    if (xvec) {
+      // 4-byte elements, nC % 4 == 0, 16-byte aligned x: 16-byte vectors
+      constexpr int V4 = TT * KC / 4;
+      for (int e = tid; e < V4; e += blockDim.x) {
+        const int r = e / (KC / 4), c = (e - r * (KC / 4)) * 4;
+        const int64_t tok = t0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tok < T && k0 + c < nC) v = __ldg(reinterpret_cast<const float4 *>(x + tok * nC + k0 + c));
+        *reinterpret_cast<float4 *>(xs + r * XSW + c) = v;
+      }
+    } else {
+      for (int e = tid; e < TT * KC; e += blockDim.x) {
+        const int r = e / KC, c = e - r * KC;
+        const int64_t tok = t0 + r;
+        float v = 0.f;
+        if (tok < T && k0 + c < nC) v = to_f(x[tok * nC + k0 + c]);
+        xs[r * XSW + c] = v;
+      }
     }
+    // dm scaled by the token's 1/rms: dx = (inv dm) . phi^T, dphi = x^T (inv dm)
     for (int e = tid; e < TT * FD; e += blockDim.x) {
       const int r = e / FD;
       const int64_t tok = t0 + r;
-      dms[e] = tok < T ? dm_ws[t0 * FD + e] : 0.f;
+      dms[e] = tok < T ? dm_ws[t0 * FD + e] * inv_rms[tok] : 0.f;
     }
     for (int e = tid; e < TT; e += blockDim.x) {
       const int64_t tok = t0 + e;
-      tinv[e] = tok < T ? inv_rms[tok] : 0.f;
       trow[e] = tok < T ? rowb_ws[tok] : 0.f;
     }
     for (int e = tid; e < TT * N; e += blockDim.x) {
@@ -411,31 +446,335 @@ dx_dphi_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restric
 #pragma unroll
           for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], pcol[j], a);
         }
-        float v = tinv[row] * a - trow[row] * xs[row * XSW + kk];
+        float v = a - trow[row] * xs[row * XSW + kk];
         v = fmaf(tgate[row * N + stream_i], dzv[r], v);
         v += dav[r];
         dx[tok * nC + kglob] = from_f<Tx>(v);
       }
     }
-    // dphi[k, j] += sum_t (x * inv)[t, k] * dm[t, j] for this thread's
-    // consecutive columns j = jgrp * RJ + q
-#pragma unroll 4
-    for (int t = 0; t < TT; ++t) {
-      const float xn = xs[t * XSW + kk] * tinv[t];
+    if constexpr (Cf::RT) {
+      // dphi[k, j] += sum_t x[t, k] (inv dm)[t, j]: 2 columns x JR projection
+      // columns per thread, the tile's tokens split over TG warp groups (one
+      // 8-byte x load and JR/4 broadcast dm loads per 2*JR FMAs)
+#pragma unroll 2
+      for (int u = 0; u < TT / TG; ++u) {
+        const int t = tg + TG * u;
+        const float2 x2 = *reinterpret_cast<const float2 *>(xs + t * XSW + 2 * lane);
+        const float *drow = dms + t * FD + jh * JR;
+        if constexpr (JR % 4 == 0 && FD % 4 == 0) {
 #pragma unroll
-      for (int q = 0; q < RJ; ++q) {
-        const int j = jgrp * RJ + q;
-        if (j < FD) acc[q] = fmaf(xn, dms[t * FD + j], acc[q]);
+          for (int q = 0; q < JR; q += 4) {
+            const float4 d4 = *reinterpret_cast<const float4 *>(drow + q);
+            acc[q] = fmaf(x2.x, d4.x, acc[q]);
+            acc[q + 1] = fmaf(x2.x, d4.y, acc[q + 1]);
+            acc[q + 2] = fmaf(x2.x, d4.z, acc[q + 2]);
+            acc[q + 3] = fmaf(x2.x, d4.w, acc[q + 3]);
+            acc[JR + q] = fmaf(x2.y, d4.x, acc[JR + q]);
+            acc[JR + q + 1] = fmaf(x2.y, d4.y, acc[JR + q + 1]);
+            acc[JR + q + 2] = fmaf(x2.y, d4.z, acc[JR + q + 2]);
+            acc[JR + q + 3] = fmaf(x2.y, d4.w, acc[JR + q + 3]);
+          }
+        } else if constexpr (JR % 2 == 0 && FD % 2 == 0) {
+#pragma unroll
+          for (int q = 0; q < JR; q += 2) {
+            const float2 d2 = *reinterpret_cast<const float2 *>(drow + q);
+            acc[q] = fmaf(x2.x, d2.x, acc[q]);
+            acc[q + 1] = fmaf(x2.x, d2.y, acc[q + 1]);
+            acc[JR + q] = fmaf(x2.y, d2.x, acc[JR + q]);
+            acc[JR + q + 1] = fmaf(x2.y, d2.y, acc[JR + q + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < JR; ++q) {
+            if (jh * JR + q < FD) {
+              const float d = drow[q];
+              acc[q] = fmaf(x2.x, d, acc[q]);
+              acc[JR + q] = fmaf(x2.y, d, acc[JR + q]);
+            }
+          }
+        }
+      }
+    } else {
+      // dphi[k, j] += sum_t x[t, k] (inv dm)[t, j] for this thread's
+      // consecutive columns j = jgrp * RJ + q
+#pragma unroll 4
+      for (int t = 0; t < TT; ++t) {
+        const float xv = xs[t * XSW + kk];
+#pragma unroll
+        for (int q = 0; q < RJ; ++q) {
+          const int j = jgrp * RJ + q;
+          if (j < FD) acc[q] = fmaf(xv, dms[t * FD + j], acc[q]);
+        }
       }
     }
   }
-  if (kvalid) {
+  if constexpr (Cf::RT) {
+    // the token groups' partials, summed in a fixed order (deterministic)
+    __syncthreads();
+    constexpr int FDP = Cf::FDP;
+    float *red = smem;  // [TG][KC][FDP]
+#pragma unroll
+    for (int q = 0; q < JR; ++q) {
+      const int j = jh * JR + q;
+      if (j < FD) {
+        red[(tg * KC + 2 * lane) * FDP + j] = acc[q];
+        red[(tg * KC + 2 * lane + 1) * FDP + j] = acc[JR + q];
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < KC * FD; e += blockDim.x) {
+      const int col = e / FD, j = e - col * FD;
+      if (k0 + col >= nC) continue;
+      float v = red[col * FDP + j];
+#pragma unroll
+      for (int g = 1; g < TG; ++g) v += red[(g * KC + col) * FDP + j];
+      dphi_part[((int64_t)blockIdx.y * nC + k0) * FD + e] = v;
+    }
+  } else if (kvalid) {
     float *dst = dphi_part + ((int64_t)blockIdx.y * nC + kglob) * FD;
 #pragma unroll
     for (int q = 0; q < RJ; ++q) {
       const int j = jgrp * RJ + q;
       if (j < FD) dst[j] = acc[q];
     }
+  }
+}
+
+// 16-byte asynchronous global -> shared copy; `bytes` < 16 fills the rest of
+// the 16 bytes with zeros (0: nothing is read, `src` need only be a valid
+// address).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int bytes) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N_>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N_) : "memory"); }
+
+template <typename Tx>
+__device__ __forceinline__ float2 ld2f(const Tx *p) {
+  if constexpr (sizeof(Tx) == 4) {
+    return *reinterpret_cast<const float2 *>(p);
+  } else {
+    return make_float2(to_f(p[0]), to_f(p[1]));
+  }
+}
+
+// The same computation as dx_dphi_kernel at KC = 64 with the tile loads
+// software-pipelined: every input of tile i+1 (x, dz, dx_add in the
+// activation dtype; dm, 1/rms, rowb, the weights in fp32) is copied into the
+// other half of a double-buffered shared-memory stage with cp.async while
+// tile i is computed, so the global-memory latency hides behind the FMAs
+// instead of stalling each tile.  Needs C % 64 == 0 (a block's 64 columns lie
+// in one stream) and 16-byte aligned x, dz, dx_add and inv_rms.
+template <int N, int MODE, typename Tx>
+struct PipeCfg {
+  using Cf = DxDphiCfg<N, MODE>;
+  static constexpr int FD = Cf::FD, KC = 64, TT = 32;
+  static constexpr int XB = TT * KC * (int)sizeof(Tx);  // one x / dz / dx_add tile (bytes)
+  static constexpr int DMB = ((TT * FD * 4 + 15) / 16) * 16, VB = TT * 4, GB = ((TT * N * 4 + 15) / 16) * 16;
+  static constexpr int SB = 3 * XB + DMB + 2 * VB + GB;  // one stage
+  static constexpr int PHI = FD * KC * 4;
+  static constexpr int BYTES = PHI + 2 * SB > Cf::RED * 4 ? PHI + 2 * SB : Cf::RED * 4;
+};
+
+template <int N, int MODE, typename Tx>
+__global__ void __launch_bounds__(256)
+dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restrict__ phi, int pdt,
+                    const float *__restrict__ inv_rms, const float *__restrict__ dm_ws,
+                    const float *__restrict__ rowb_ws, const float *__restrict__ gate_ws,
+                    const Tx *__restrict__ dz, const Tx *__restrict__ dx_add, Tx *__restrict__ dx,
+                    float *__restrict__ dphi_part, int tsplits) {
+  using Cf = DxDphiCfg<N, MODE>;
+  using Pc = PipeCfg<N, MODE, Tx>;
+  static_assert(Cf::RT && Cf::KC == 64, "pipelined path: 64 columns per block");
+  constexpr int FD = Cf::FD, KC = 64, TT = 32, JH = Cf::JH, JR = Cf::JR, TG = Cf::TG;
+  constexpr int JGRP = 256 / KC, RR = TT / JGRP;
+  constexpr int EPV = 16 / (int)sizeof(Tx);   // elements per 16-byte vector
+  constexpr int VPR = KC / EPV;               // vectors per tile row
+  extern __shared__ float4 smem4[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>(smem4);
+  float *psT = reinterpret_cast<float *>(sm);  // [FD][KC]
+  auto stage = [&](int b) { return sm + Pc::PHI + b * Pc::SB; };
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kk = tid % KC, jgrp = tid / KC;
+  const int64_t nC = (int64_t)N * C;
+  const int64_t k0 = (int64_t)blockIdx.x * KC;
+  const int64_t kglob = k0 + kk;
+  const int stream_i = (int)(k0 / C);
+  const int c0 = (int)(k0 - (int64_t)stream_i * C);
+  const int jh = warp % JH, tg = warp / JH;
+
+  const int64_t tiles = (T + TT - 1) / TT;
+  const int64_t tiles_per = (tiles + tsplits - 1) / tsplits;
+  const int64_t tile_beg = (int64_t)blockIdx.y * tiles_per;
+  int64_t tile_end = tile_beg + tiles_per;
+  if (tile_end > tiles) tile_end = tiles;
+
+  // all inputs of one tile into stage b (one commit group)
+  auto issue = [&](int64_t tile, int b) {
+    uint8_t *st = stage(b);
+    uint8_t *xb = st, *zb = st + Pc::XB, *ab = st + 2 * Pc::XB, *db = st + 3 * Pc::XB;
+    uint8_t *ib = db + Pc::DMB, *rb = ib + Pc::VB, *gb = rb + Pc::VB;
+    const int64_t t0 = tile * TT;
+    for (int e = tid; e < TT * VPR; e += 256) {
+      const int r = e / VPR, v = e - r * VPR;
+      const int64_t tok = t0 + r;
+      const bool ok = tok < T;
+      const int64_t tk = ok ? tok : 0;
+      const int nb = ok ? 16 : 0;
+      cp_async16(xb + (r * VPR + v) * 16, x + tk * nC + k0 + v * EPV, nb);
+      cp_async16(zb + (r * VPR + v) * 16, dz + tk * C + c0 + v * EPV, nb);
+      if (dx_add) cp_async16(ab + (r * VPR + v) * 16, dx_add + tk * nC + k0 + v * EPV, nb);
+    }
+    const int64_t dm_total = T * FD, dm0 = t0 * FD;
+    for (int e = tid; e < Pc::DMB / 16; e += 256) {
+      const int64_t left = dm_total - (dm0 + 4 * e);
+      const int nb = left >= 4 ? 16 : (left > 0 ? (int)left * 4 : 0);
+      cp_async16(db + e * 16, dm_ws + (nb ? dm0 + 4 * e : 0), nb);
+    }
+    for (int e = tid; e < TT / 4; e += 256) {
+      const int64_t left = T - (t0 + 4 * e);
+      const int nb = left >= 4 ? 16 : (left > 0 ? (int)left * 4 : 0);
+      cp_async16(ib + e * 16, inv_rms + (nb ? t0 + 4 * e : 0), nb);
+      cp_async16(rb + e * 16, rowb_ws + (nb ? t0 + 4 * e : 0), nb);
+    }
+    const int64_t g_total = T * N, g0 = t0 * N;
+    for (int e = tid; e < Pc::GB / 16; e += 256) {
+      const int64_t left = g_total - (g0 + 4 * e);
+      const int nb = left >= 4 ? 16 : (left > 0 ? (int)left * 4 : 0);
+      cp_async16(gb + e * 16, gate_ws + (nb ? g0 + 4 * e : 0), nb);
+    }
+    cp_async_commit();
+  };
+
+  if (tile_beg < tile_end) issue(tile_beg, 0);
+  for (int e = tid; e < KC * FD; e += blockDim.x) {
+    const int r = e / FD, j = e - r * FD;
+    psT[j * KC + r] = load_dyn(phi, pdt, (k0 + r) * FD + j);
+  }
+  __syncthreads();
+  constexpr bool PREG = FD <= 32;
+  float pcol[PREG ? FD : 1];
+  if constexpr (PREG) {
+#pragma unroll
+    for (int j = 0; j < FD; ++j) pcol[j] = psT[j * KC + kk];
+  }
+  float acc[2 * JR];
+#pragma unroll
+  for (int q = 0; q < 2 * JR; ++q) acc[q] = 0.f;
+
+  int b = 0;
+  for (int64_t tile = tile_beg; tile < tile_end; ++tile, b ^= 1) {
+    __syncthreads();  // every thread is done with stage b ^ 1 (the previous tile)
+    if (tile + 1 < tile_end) {
+      issue(tile + 1, b ^ 1);
+      cp_async_wait<1>();  // this tile's group has landed (the next may be in flight)
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint8_t *st = stage(b);
+    const Tx *xs = reinterpret_cast<const Tx *>(st);
+    const Tx *zs = reinterpret_cast<const Tx *>(st + Pc::XB);
+    const Tx *as = reinterpret_cast<const Tx *>(st + 2 * Pc::XB);
+    const float *dms = reinterpret_cast<const float *>(st + 3 * Pc::XB);
+    const float *tinv = reinterpret_cast<const float *>(st + 3 * Pc::XB + Pc::DMB);
+    const float *trow = tinv + TT;
+    const float *tgate = trow + TT;
+    const int64_t t0 = tile * TT;
+    // dx for rows jgrp + JGRP*r, column kk
+#pragma unroll 2
+    for (int r = 0; r < RR; ++r) {
+      const int row = jgrp + JGRP * r;
+      const int64_t tok = t0 + row;
+      if (tok >= T) continue;
+      float a = 0.f;
+      if constexpr (!PREG) {
+#pragma unroll 8
+        for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
+      } else if constexpr (FD % 4 == 0) {
+#pragma unroll
+        for (int j = 0; j < FD; j += 4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(dms + row * FD + j);  // one row: broadcast
+          a = fmaf(d4.x, pcol[j], a);
+          a = fmaf(d4.y, pcol[j + 1], a);
+          a = fmaf(d4.z, pcol[j + 2], a);
+          a = fmaf(d4.w, pcol[j + 3], a);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], pcol[j], a);
+      }
+      float v = tinv[row] * a - trow[row] * to_f(xs[row * KC + kk]);
+      v = fmaf(tgate[row * N + stream_i], to_f(zs[row * KC + kk]), v);
+      if (dx_add) v += to_f(as[row * KC + kk]);
+      dx[tok * nC + kglob] = from_f<Tx>(v);
+    }
+    // dphi[k, j] += sum_t (x * inv)[t, k] dm[t, j]: 2 columns x JR projection
+    // columns per thread, the tile's tokens split over TG warp groups
+#pragma unroll 2
+    for (int u = 0; u < TT / TG; ++u) {
+      const int t = tg + TG * u;
+      float2 x2 = ld2f(xs + t * KC + 2 * lane);
+      const float iv = tinv[t];
+      x2.x *= iv;
+      x2.y *= iv;
+      const float *drow = dms + t * FD + jh * JR;
+      if constexpr (JR % 4 == 0 && FD % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < JR; q += 4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(drow + q);
+          acc[q] = fmaf(x2.x, d4.x, acc[q]);
+          acc[q + 1] = fmaf(x2.x, d4.y, acc[q + 1]);
+          acc[q + 2] = fmaf(x2.x, d4.z, acc[q + 2]);
+          acc[q + 3] = fmaf(x2.x, d4.w, acc[q + 3]);
+          acc[JR + q] = fmaf(x2.y, d4.x, acc[JR + q]);
+          acc[JR + q + 1] = fmaf(x2.y, d4.y, acc[JR + q + 1]);
+          acc[JR + q + 2] = fmaf(x2.y, d4.z, acc[JR + q + 2]);
+          acc[JR + q + 3] = fmaf(x2.y, d4.w, acc[JR + q + 3]);
+        }
+      } else if constexpr (JR % 2 == 0 && FD % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < JR; q += 2) {
+          const float2 d2 = *reinterpret_cast<const float2 *>(drow + q);
+          acc[q] = fmaf(x2.x, d2.x, acc[q]);
+          acc[q + 1] = fmaf(x2.x, d2.y, acc[q + 1]);
+          acc[JR + q] = fmaf(x2.y, d2.x, acc[JR + q]);
+          acc[JR + q + 1] = fmaf(x2.y, d2.y, acc[JR + q + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < JR; ++q) {
+          if (jh * JR + q < FD) {
+            const float d = drow[q];
+            acc[q] = fmaf(x2.x, d, acc[q]);
+            acc[JR + q] = fmaf(x2.y, d, acc[JR + q]);
+          }
+        }
+      }
+    }
+  }
+  // the token groups' partials, summed in a fixed order (deterministic)
+  __syncthreads();
+  constexpr int FDP = Cf::FDP;
+  float *red = reinterpret_cast<float *>(sm);  // [TG][KC][FDP]
+#pragma unroll
+  for (int q = 0; q < JR; ++q) {
+    const int j = jh * JR + q;
+    if (j < FD) {
+      red[(tg * KC + 2 * lane) * FDP + j] = acc[q];
+      red[(tg * KC + 2 * lane + 1) * FDP + j] = acc[JR + q];
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < KC * FD; e += blockDim.x) {
+    const int col = e / FD, j = e - col * FD;
+    float v = red[col * FDP + j];
+#pragma unroll
+    for (int g = 1; g < TG; ++g) v += red[(g * KC + col) * FDP + j];
+    dphi_part[((int64_t)blockIdx.y * nC + k0) * FD + e] = v;
   }
 }
 
@@ -532,16 +871,34 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
                                   dx_add, dx, dphi_part, splits, stream);
             if (e != cudaSuccess) return e;
           } else {
-          constexpr int KC = FD <= 96 ? 64 : 16;
-          const size_t smem2 = ((size_t)FD * KC + 32 * (KC + 1) + 32 * FD + 64 + 32 * N) * 4;
-          auto k2 = dx_dphi_kernel<N, MODE, Tx>;
-          e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
-          if (e != cudaSuccess) return e;
-          dim3 grid2(plan.k2_kblocks, plan.k2_tsplits);
-          k2<<<grid2, 256, smem2, stream>>>((const Tx *)x, T, C, phi, p.param_dtype, inv_rms, dm_ws,
-                                            rowb_ws, gate_ws, (const Tx *)dz, (const Tx *)dx_add,
-                                            (Tx *)dx, dphi_part, plan.k2_tsplits);
-          if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            dim3 grid2(plan.k2_kblocks, plan.k2_tsplits);
+            bool done = false;
+            if constexpr (DxDphiCfg<N, MODE>::RT) {
+              const bool pipe = C % 64 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)dz & 15) == 0 &&
+                                ((uintptr_t)dx_add & 15) == 0 && ((uintptr_t)inv_rms & 15) == 0;
+              if (pipe) {
+                const size_t smemp = (size_t)PipeCfg<N, MODE, Tx>::BYTES;
+                auto kp = dx_dphi_pipe_kernel<N, MODE, Tx>;
+                e = cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smemp);
+                if (e != cudaSuccess) return e;
+                kp<<<grid2, 256, smemp, stream>>>((const Tx *)x, T, C, phi, p.param_dtype, inv_rms, dm_ws,
+                                                  rowb_ws, gate_ws, (const Tx *)dz, (const Tx *)dx_add, (Tx *)dx,
+                                                  dphi_part, plan.k2_tsplits);
+                if ((e = cudaGetLastError()) != cudaSuccess) return e;
+                done = true;
+              }
+            }
+            if (!done) {
+              const size_t smem2 = (size_t)DxDphiCfg<N, MODE>::SMEM_FLOATS * 4;
+              const bool xvec = sizeof(Tx) == 4 && nC % 4 == 0 && ((uintptr_t)x & 15) == 0;
+              auto k2 = dx_dphi_kernel<N, MODE, Tx>;
+              e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+              if (e != cudaSuccess) return e;
+              k2<<<grid2, 256, smem2, stream>>>((const Tx *)x, T, C, phi, p.param_dtype, inv_rms, dm_ws,
+                                                rowb_ws, gate_ws, (const Tx *)dz, (const Tx *)dx_add,
+                                                (Tx *)dx, dphi_part, plan.k2_tsplits, xvec);
+              if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            }
           }
         }
         // K3
