@@ -24,6 +24,7 @@
 #include "mhc_device.cuh"
 #include "mhc_dispatch.cuh"
 #include "mhc_kernels.h"
+#include "mhc_sm100.cuh"
 
 namespace mhc {
 
@@ -579,7 +580,9 @@ struct PipeCfg {
 };
 
 template <int N, int MODE, typename Tx>
-__global__ void __launch_bounds__(256)
+// three blocks per SM (24 warps to hide the FMA chains) where a thread's
+// dphi accumulators (2 x JR) fit in 80 registers with the rest, else two
+__global__ void __launch_bounds__(256, (DxDphiCfg<N, MODE>::JR <= 12 ? 3 : 2))
 dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restrict__ phi, int pdt,
                     const float *__restrict__ inv_rms, const float *__restrict__ dm_ws,
                     const float *__restrict__ rowb_ws, const float *__restrict__ gate_ws,
@@ -656,14 +659,28 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
   }
   __syncthreads();
   constexpr bool PREG = FD <= 32;
+  // packed fp32 pairs (fma.rn.f32x2, two FMAs per instruction) where the
+  // widths allow: dx's dm . phi over j pairs, dphi over projection-column pairs
+  constexpr bool PAIR = PREG && FD % 4 == 0 && JR % 4 == 0;
+  using sm100::f2_fma;
+  using sm100::f2_pack;
+  using sm100::f2_unpack;
   float pcol[PREG ? FD : 1];
   if constexpr (PREG) {
 #pragma unroll
     for (int j = 0; j < FD; ++j) pcol[j] = psT[j * KC + kk];
   }
+  uint64_t pc2[PAIR ? FD / 2 : 1];
+  if constexpr (PAIR) {
+#pragma unroll
+    for (int j = 0; j < FD / 2; ++j) pc2[j] = f2_pack(pcol[2 * j], pcol[2 * j + 1]);
+  }
   float acc[2 * JR];
 #pragma unroll
   for (int q = 0; q < 2 * JR; ++q) acc[q] = 0.f;
+  uint64_t acc2[PAIR ? JR : 1];  // [column][q/2]: projection columns q, q+1 of column 2*lane + column
+#pragma unroll
+  for (int q = 0; q < (PAIR ? JR : 1); ++q) acc2[q] = f2_pack(0.f, 0.f);
 
   int b = 0;
   for (int64_t tile = tile_beg; tile < tile_end; ++tile, b ^= 1) {
@@ -691,7 +708,20 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
       const int64_t tok = t0 + row;
       if (tok >= T) continue;
       float a = 0.f;
-      if constexpr (!PREG) {
+      if constexpr (PAIR) {
+        // even and odd j in the two halves of two packed accumulators
+        uint64_t s0 = f2_pack(0.f, 0.f), s1 = s0;
+#pragma unroll
+        for (int j = 0; j < FD; j += 4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(dms + row * FD + j);  // one row: broadcast
+          s0 = f2_fma(f2_pack(d4.x, d4.y), pc2[j / 2], s0);
+          s1 = f2_fma(f2_pack(d4.z, d4.w), pc2[j / 2 + 1], s1);
+        }
+        float a0, a1, a2, a3;
+        f2_unpack(s0, a0, a1);
+        f2_unpack(s1, a2, a3);
+        a = (a0 + a1) + (a2 + a3);
+      } else if constexpr (!PREG) {
 #pragma unroll 8
         for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
       } else if constexpr (FD % 4 == 0) {
@@ -722,7 +752,18 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
       x2.x *= iv;
       x2.y *= iv;
       const float *drow = dms + t * FD + jh * JR;
-      if constexpr (JR % 4 == 0 && FD % 4 == 0) {
+      if constexpr (PAIR) {
+        const uint64_t xa = f2_pack(x2.x, x2.x), xb = f2_pack(x2.y, x2.y);
+#pragma unroll
+        for (int q = 0; q < JR; q += 4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(drow + q);
+          const uint64_t p0 = f2_pack(d4.x, d4.y), p1 = f2_pack(d4.z, d4.w);
+          acc2[q / 2] = f2_fma(xa, p0, acc2[q / 2]);
+          acc2[q / 2 + 1] = f2_fma(xa, p1, acc2[q / 2 + 1]);
+          acc2[JR / 2 + q / 2] = f2_fma(xb, p0, acc2[JR / 2 + q / 2]);
+          acc2[JR / 2 + q / 2 + 1] = f2_fma(xb, p1, acc2[JR / 2 + q / 2 + 1]);
+        }
+      } else if constexpr (JR % 4 == 0 && FD % 4 == 0) {
 #pragma unroll
         for (int q = 0; q < JR; q += 4) {
           const float4 d4 = *reinterpret_cast<const float4 *>(drow + q);
@@ -754,6 +795,13 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
           }
         }
       }
+    }
+  }
+  if constexpr (PAIR) {
+#pragma unroll
+    for (int q = 0; q < JR; q += 2) {
+      f2_unpack(acc2[q / 2], acc[q], acc[q + 1]);
+      f2_unpack(acc2[JR / 2 + q / 2], acc[JR + q], acc[JR + q + 1]);
     }
   }
   // the token groups' partials, summed in a fixed order (deterministic)
