@@ -531,6 +531,29 @@ def run_post_pre(args, rank, world, local_rank):
                       "peak_kind": peak_kind, "post_pre": e}))
 
 
+def run_fp32_stream(args, rank, world, local_rank):
+    """--workload fp32_stream: the layer with an fp32 residual stream and a bf16
+    sublayer output (the reference trainers' bf16-autocast setting), forward
+    and backward, K steps each after W warm-ups, at --tokens per GPU."""
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = _peaks()
+    c = args.C or 768
+    lb = LayerBench(args.tokens, 4, c, args.variant == "full", torch.float32, torch.bfloat16, dev, stream, 77 + rank)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    e = _layer_entry(lb, world, dev, args.steps, args.warmup, stream, peak, flush, not args.no_bwd, 4, 2)
+    if rank != 0:
+        return
+    print(json.dumps({"metric": "mHC layer tokens/s", "value": e["tokens_per_s"], "unit": "tokens/s",
+                      "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": e["ms_per_step"],
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic",
+                      "config": {"workload": f"fp32 stream: x fp32, f bf16, {args.tokens} tokens/GPU, C={c}, n=4, "
+                                             f"{args.variant}", "l2": e["l2"]},
+                      "peak_kind": peak_kind, "fp32_stream": e}))
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -1268,9 +1291,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["layer", "c4", "c5", "post_pre"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "c4", "c5", "post_pre", "fp32_stream"], default="layer",
                     help="layer: configs[1] mHC layer (the headline); c4 / c5: model-level configs[3] / [4]; "
-                         "post_pre: the step between two sublayers, two kernels against the fused kernel")
+                         "post_pre: the step between two sublayers, two kernels against the fused kernel; "
+                         "fp32_stream: the layer with an fp32 residual stream (forward and backward)")
     ap.add_argument("--variant", choices=["full", "nohres"], default="full")
     ap.add_argument("--C", type=int, default=0, help="stream width for --variant nohres (768 or 1024)")
     ap.add_argument("--tokens", type=int, default=16 * 2048)
@@ -1310,6 +1334,8 @@ def main():
             run_ours(args, rank, world, local_rank)
         elif args.workload == "post_pre":
             run_post_pre(args, rank, world, local_rank)
+        elif args.workload == "fp32_stream":
+            run_fp32_stream(args, rank, world, local_rank)
         else:
             run_model(args, rank, world, local_rank)
     finally:
