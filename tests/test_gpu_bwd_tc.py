@@ -78,3 +78,65 @@ def test_tc_backward_full_size_repeatable():
     assert torch.equal(dx1, dx2)
     for a, b in zip(g1, g2):
         assert torch.equal(a, b)
+
+
+def test_tc_backward_full_size_vs_oracle_and_linear_in_tokens():
+    """32,768 tokens at config 2 through the tensor-core backward.
+
+    dx of a token depends only on that token's inputs, so 256 sampled tokens
+    are checked against oracle autograd (fp32 on the same bf16 inputs,
+    model/mhc_fused.py:533-559 with Sinkhorn, then the backward of
+    <dz, z> + <dh_post, h_post> + <dh_res, H_res> plus dx_add).  dphi is a sum
+    over tokens: the full batch's equals the sum over four 8,192-token chunks
+    run separately, and every chunk's dx equals the full run's rows bit for bit.
+    """
+    from model import _native as nat
+    from model.mhc_fused import _params, _pre_bwd, _pre_fwd
+    from oracle import mhc_oracle as O
+    L = nat.lib()
+    n, c, t, iters = 4, 768, 16 * 2048, 20
+    gen = torch.Generator().manual_seed(21)
+    fd = 2 * n + n * n
+    raw = [torch.randn(n * c, fd, generator=gen) * 0.02, torch.tensor(0.3), torch.randn(n, generator=gen) * 0.1,
+           torch.tensor(0.2), torch.randn(n, generator=gen) * 0.1, torch.tensor(0.25),
+           torch.eye(n) + torch.randn(n, n, generator=gen) * 0.1]
+    ps = _params(*[r.to(DEV) for r in raw])
+    torch.manual_seed(21)
+    x = torch.randn(t, n * c, device=DEV).bfloat16()
+    dz = torch.randn(t, c, device=DEV).bfloat16()
+    dh_post = torch.randn(t, n, device=DEV)
+    dh_res = torch.randn(t, n * n, device=DEV)
+    dx_add = torch.randn(t, n * c, device=DEV).bfloat16()
+    _, _, _, _, inv, mixes = _pre_fwd(x, ps, True, True, iters, 2.0, 1e-6, 1e-6, 1e-6, n, c, torch.float32, False)
+
+    def bwd(sl):
+        return _pre_bwd(x[sl], ps, True, True, iters, 2.0, 1e-6, 1e-6, 1e-6, n, c, inv[sl], mixes[sl], dz[sl], None,
+                        dh_post[sl], dh_res[sl], torch.float32, dx_add[sl])
+
+    prev = L.mhc_set_path_policy(0)
+    try:
+        dx, gps = bwd(slice(0, t))
+        assert L.mhc_last_path() == 1, "the tensor-core backward did not run"
+        chunk = t // 4
+        dphi_sum = torch.zeros_like(gps[0])
+        for k in range(4):
+            sl = slice(k * chunk, (k + 1) * chunk)
+            dxk, gk = bwd(sl)
+            assert torch.equal(dxk, dx[sl])
+            dphi_sum += gk[0]
+    finally:
+        L.mhc_set_path_policy(prev)
+    torch.cuda.synchronize()
+    assert L.mhc_device_error(1) == 0
+    assert max_rel(gps[0], dphi_sum) < 1e-5
+
+    idx = torch.randperm(t, generator=gen)[:256].to(DEV)
+    p = [r.float() for r in raw]
+    xo = x[idx].float().cpu().requires_grad_(True)
+    z, _, h_post, h_res_raw, _, _ = O.pre_phase_full(xo, p[0], p[1], p[2], p[3], p[4], p[5], p[6], 2.0, 1e-6,
+                                                     1e-6, n, c)
+    h_res = O.sinkhorn(h_res_raw, iters, 1e-6)
+    (gx,) = torch.autograd.grad([z, h_post, h_res], [xo],
+                                [dz[idx].float().cpu(), dh_post[idx].cpu(), dh_res[idx].cpu().view(-1, n, n)])
+    ref = gx + dx_add[idx].float().cpu()
+    assert max_rel(ref, dx[idx]) < 2e-2
