@@ -88,7 +88,6 @@ constexpr int CHUNK = TM * QC * 2;   // one ring slot: 128 rows x 32 bf16, 64-by
 constexpr int CHUNK_F = TM * QC * 4; // fp32 streams: 128 rows x 32 fp32, 128-byte swizzle
 constexpr int RING_MAX = 24;
 constexpr int S_MIN = 4, S_MAX = 8;  // cluster sizes (C = 128 S)
-constexpr int TPC_MAX = 32;          // tokens a CTA owns per tile: ceil(128 / S)
 constexpr int NZW = 8, NMW = 4;      // pre-aggregate warps, merge warps
 constexpr int W_PROD = 0, W_MMA = 1, W_ROW = 2, W_COEF = 6, W_SK = 7, W_Z = 8, W_MRG = 16;
 constexpr int W_CONV = 2;            // first warp that converts phi in the prologue
