@@ -561,6 +561,16 @@ __device__ __forceinline__ float2 ld2f(const Tx *p) {
   }
 }
 
+template <typename Tx>
+__device__ __forceinline__ void st2(Tx *p, float a, float b) {
+  if constexpr (sizeof(Tx) == 4) {
+    *reinterpret_cast<float2 *>(p) = make_float2(a, b);
+  } else {
+    Tx h[2] = {from_f<Tx>(a), from_f<Tx>(b)};
+    *reinterpret_cast<uint32_t *>(p) = *reinterpret_cast<const uint32_t *>(h);
+  }
+}
+
 // The same computation as dx_dphi_kernel at KC = 64 with the tile loads
 // software-pipelined: every input of tile i+1 (x, dz, dx_add in the
 // activation dtype; dm, 1/rms, rowb, the weights in fp32) is copied into the
@@ -577,12 +587,15 @@ struct PipeCfg {
   static constexpr int SB = 3 * XB + DMB + 2 * VB + GB;  // one stage
   static constexpr int PHI = FD * KC * 4;
   static constexpr int BYTES = PHI + 2 * SB > Cf::RED * 4 ? PHI + 2 * SB : Cf::RED * 4;
+  // packed fp32 pairs (fma.rn.f32x2) where the widths allow; then a thread's
+  // dx is two adjacent columns (one dm row broadcast serves both)
+  static constexpr bool PAIR = FD <= 32 && FD % 4 == 0 && Cf::JR % 4 == 0;
+  // blocks per SM the registers are sized for
+  static constexpr int MINB = PAIR ? 2 : (Cf::JR <= 12 ? 3 : 2);
 };
 
 template <int N, int MODE, typename Tx>
-// three blocks per SM (24 warps to hide the FMA chains) where a thread's
-// dphi accumulators (2 x JR) fit in 80 registers with the rest, else two
-__global__ void __launch_bounds__(256, (DxDphiCfg<N, MODE>::JR <= 12 ? 3 : 2))
+__global__ void __launch_bounds__(256, (PipeCfg<N, MODE, Tx>::MINB))
 dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__restrict__ phi, int pdt,
                     const float *__restrict__ inv_rms, const float *__restrict__ dm_ws,
                     const float *__restrict__ rowb_ws, const float *__restrict__ gate_ws,
@@ -660,20 +673,25 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
   __syncthreads();
   constexpr bool PREG = FD <= 32;
   // packed fp32 pairs (fma.rn.f32x2, two FMAs per instruction) where the
-  // widths allow: dx's dm . phi over j pairs, dphi over projection-column pairs
-  constexpr bool PAIR = PREG && FD % 4 == 0 && JR % 4 == 0;
+  // widths allow: dx's dm . phi over j pairs for two adjacent columns per
+  // thread, dphi over projection-column pairs
+  constexpr bool PAIR = Pc::PAIR;
   using sm100::f2_fma;
   using sm100::f2_pack;
   using sm100::f2_unpack;
-  float pcol[PREG ? FD : 1];
-  if constexpr (PREG) {
+  float pcol[(PREG && !PAIR) ? FD : 1];
+  if constexpr (PREG && !PAIR) {
 #pragma unroll
     for (int j = 0; j < FD; ++j) pcol[j] = psT[j * KC + kk];
   }
-  uint64_t pc2[PAIR ? FD / 2 : 1];
+  // phi of columns 2*lane (A) and 2*lane + 1 (B) as (j, j+1) pairs
+  uint64_t pcA[PAIR ? FD / 2 : 1], pcB[PAIR ? FD / 2 : 1];
   if constexpr (PAIR) {
 #pragma unroll
-    for (int j = 0; j < FD / 2; ++j) pc2[j] = f2_pack(pcol[2 * j], pcol[2 * j + 1]);
+    for (int j = 0; j < FD / 2; ++j) {
+      pcA[j] = f2_pack(psT[(2 * j) * KC + 2 * lane], psT[(2 * j + 1) * KC + 2 * lane]);
+      pcB[j] = f2_pack(psT[(2 * j) * KC + 2 * lane + 1], psT[(2 * j + 1) * KC + 2 * lane + 1]);
+    }
   }
   float acc[2 * JR];
 #pragma unroll
@@ -701,27 +719,55 @@ dx_dphi_pipe_kernel(const Tx *__restrict__ x, int64_t T, int C, const void *__re
     const float *trow = tinv + TT;
     const float *tgate = trow + TT;
     const int64_t t0 = tile * TT;
+    if constexpr (PAIR) {
+      // dx for columns 2*lane, 2*lane + 1 and rows warp + 8r: one broadcast of
+      // the row's dm serves both columns; even and odd j accumulate in the two
+      // halves of two packed accumulators per column
+#pragma unroll 2
+      for (int r = 0; r < TT / 8; ++r) {
+        const int row = warp + 8 * r;
+        const int64_t tok = t0 + row;
+        if (tok >= T) continue;
+        uint64_t sa0 = f2_pack(0.f, 0.f), sa1 = sa0, sb0 = sa0, sb1 = sa0;
+#pragma unroll
+        for (int j = 0; j < FD; j += 4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(dms + row * FD + j);  // one row: broadcast
+          const uint64_t p01 = f2_pack(d4.x, d4.y), p23 = f2_pack(d4.z, d4.w);
+          sa0 = f2_fma(p01, pcA[j / 2], sa0);
+          sa1 = f2_fma(p23, pcA[j / 2 + 1], sa1);
+          sb0 = f2_fma(p01, pcB[j / 2], sb0);
+          sb1 = f2_fma(p23, pcB[j / 2 + 1], sb1);
+        }
+        float u0, u1, u2, u3;
+        f2_unpack(sa0, u0, u1);
+        f2_unpack(sa1, u2, u3);
+        const float aA = (u0 + u1) + (u2 + u3);
+        f2_unpack(sb0, u0, u1);
+        f2_unpack(sb1, u2, u3);
+        const float aB = (u0 + u1) + (u2 + u3);
+        const float2 x2 = ld2f(xs + row * KC + 2 * lane);
+        const float2 z2 = ld2f(zs + row * KC + 2 * lane);
+        const float iv = tinv[row], rb = trow[row], gw = tgate[row * N + stream_i];
+        float vA = iv * aA - rb * x2.x;
+        float vB = iv * aB - rb * x2.y;
+        vA = fmaf(gw, z2.x, vA);
+        vB = fmaf(gw, z2.y, vB);
+        if (dx_add) {
+          const float2 a2 = ld2f(as + row * KC + 2 * lane);
+          vA += a2.x;
+          vB += a2.y;
+        }
+        st2(dx + tok * nC + k0 + 2 * lane, vA, vB);
+      }
+    }
     // dx for rows jgrp + JGRP*r, column kk
 #pragma unroll 2
-    for (int r = 0; r < RR; ++r) {
+    for (int r = 0; r < (PAIR ? 0 : RR); ++r) {
       const int row = jgrp + JGRP * r;
       const int64_t tok = t0 + row;
       if (tok >= T) continue;
       float a = 0.f;
-      if constexpr (PAIR) {
-        // even and odd j in the two halves of two packed accumulators
-        uint64_t s0 = f2_pack(0.f, 0.f), s1 = s0;
-#pragma unroll
-        for (int j = 0; j < FD; j += 4) {
-          const float4 d4 = *reinterpret_cast<const float4 *>(dms + row * FD + j);  // one row: broadcast
-          s0 = f2_fma(f2_pack(d4.x, d4.y), pc2[j / 2], s0);
-          s1 = f2_fma(f2_pack(d4.z, d4.w), pc2[j / 2 + 1], s1);
-        }
-        float a0, a1, a2, a3;
-        f2_unpack(s0, a0, a1);
-        f2_unpack(s1, a2, a3);
-        a = (a0 + a1) + (a2 + a3);
-      } else if constexpr (!PREG) {
+      if constexpr (!PREG) {
 #pragma unroll 8
         for (int j = 0; j < FD; ++j) a = fmaf(dms[row * FD + j], psT[j * KC + kk], a);
       } else if constexpr (FD % 4 == 0) {
@@ -923,7 +969,8 @@ cudaError_t launch_pre_bwd(int mode, int n, int x_dtype, const void *x, int64_t 
             bool done = false;
             if constexpr (DxDphiCfg<N, MODE>::RT) {
               const bool pipe = C % 64 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)dz & 15) == 0 &&
-                                ((uintptr_t)dx_add & 15) == 0 && ((uintptr_t)inv_rms & 15) == 0;
+                                ((uintptr_t)dx_add & 15) == 0 && ((uintptr_t)inv_rms & 15) == 0 &&
+                                ((uintptr_t)dx & 15) == 0;
               if (pipe) {
                 const size_t smemp = (size_t)PipeCfg<N, MODE, Tx>::BYTES;
                 auto kp = dx_dphi_pipe_kernel<N, MODE, Tx>;
